@@ -1,0 +1,65 @@
+// Declarations shared by the kernel files of libnvb.so. The library is built
+// as one translation unit (nvb_unity.cu) so that the device-global error
+// word in common.cuh needs no relocatable device code.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace nvb {
+
+// Query-row modes of the decode kernel.
+enum DecodeMode : int {
+  kModeDecode = 0,  // row b is sequence b's single query; lens = kv_lens
+  kModeNative = 1,  // reference nv_attention form: lens = positions, seq_map = seq_indices
+  kModeVarlen = 2,  // one CTA per query row of a varlen batch: seq_map = cu_q, lens = kv_lens
+};
+
+struct DecodeParams {
+  const __nv_bfloat16* q;   // [rows, qh, 128]
+  __nv_bfloat16* out;       // [rows, qh, 128]
+  const int* lens;          // kv_lens[seq] (decode, varlen) or positions[row] (native)
+  const int* seq_map;       // seq_indices[row] (native) or cu_q[batch + 1] (varlen)
+  const int* block_table;   // [*, table_stride]
+  float* lse;               // optional final LSE at (seq * qh + head) * max_q + i
+  float* lse_accum;         // [splits, rows, qh]      (splits > 1)
+  float* out_accum;         // [splits, rows, qh, 128] (splits > 1)
+  int rows, qh, kvh, block_size, table_stride, num_blocks, batch, max_context;
+  int num_splits, n_hgroups, max_q;
+  int mode;
+  float scale_log2;  // log2(e) / sqrt(128)
+};
+
+cudaError_t launch_decode(DecodeParams p, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                          cudaStream_t stream);
+int decode_group_chunk(int group);
+
+cudaError_t launch_qkv_rope(cudaStream_t stream, bool cached, const void* qkv, const void* qw,
+                            const void* kw, const int* positions, const int* slots, void* qout,
+                            void* kc, void* vc, int rows, int qh, int kvh, int bs, int blocks,
+                            float eps, float theta, const float* rope_cache, int max_positions);
+cudaError_t launch_rope_cache(cudaStream_t stream, float* cache, int positions, int dim, float theta);
+
+struct PrefillArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  const int* cu_q;
+  const int* kv_lens;
+  const int* block_table;
+  float* lse;
+  int batch, total_q, max_q, max_k, qh, kvh, block_size, table_stride, num_blocks;
+};
+
+// Host-side TMA descriptor helper (api.cu): 3-D BF16 map over
+// [dims[2]][dims[1]][dims[0]], cached per thread.
+int make_map_3d(const void* base, const uint64_t dims[3], const uint64_t strides[2],
+                const uint32_t box[3], CUtensorMapSwizzle swizzle, const CUtensorMap** out);
+
+// Returns cudaErrorNotSupported when the tcgen05 path does not cover the shape.
+cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
+
+}  // namespace nvb

@@ -1,0 +1,5 @@
+// Single translation unit for libnvb.so (see internal.cuh).
+#include "api.cu"
+#include "decode.cu"
+#include "prefill.cu"
+#include "qkv_rope.cu"
