@@ -81,7 +81,7 @@ class ClockSampler(threading.Thread):
     def __init__(self, device_index):
         super().__init__(daemon=True)
         self.samples, self.reasons, self.max_mhz = [], set(), None
-        self._stop = threading.Event()
+        self._halt = threading.Event()
         self.ok = False
         try:
             import pynvml as nv
@@ -101,7 +101,7 @@ class ClockSampler(threading.Thread):
             self.err = str(e)
 
     def run(self):
-        while self.ok and not self._stop.is_set():
+        while self.ok and not self._halt.is_set():
             try:
                 self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
                 mask = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
@@ -113,7 +113,7 @@ class ClockSampler(threading.Thread):
             time.sleep(0.02)
 
     def stop(self):
-        self._stop.set()
+        self._halt.set()
         self.join(timeout=2)
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
@@ -216,6 +216,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="sequences per GPU (default 256 = config 3; smaller only for profiler captures)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -238,15 +241,16 @@ def main():
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
 
     # ---------------- device-resident decode (value, roofline)
-    case = W.config3_decode(device=dev, seed=rank)
-    splits = nvb.num_splits(BATCH, QH, KVH, CTX, sms)
+    batch = args.batch
+    case = W.config3_decode(device=dev, seed=rank, batch=batch)
+    splits = nvb.num_splits(batch, QH, KVH, CTX, sms)
     out = torch.empty_like(case.q)
-    lse = torch.empty(BATCH, QH, 1, dtype=torch.float32, device=dev)
-    la, oa = nvb.splitkv_scratch(splits, BATCH, QH, dev) if splits > 1 else (None, None)
+    lse = torch.empty(batch, QH, 1, dtype=torch.float32, device=dev)
+    la, oa = nvb.splitkv_scratch(splits, batch, QH, dev) if splits > 1 else (None, None)
     lib = nvb.library()
     stream = torch.cuda.current_stream()
     raw = [nvb._stream(stream), nvb._ptr(case.q), nvb._ptr(case.k), nvb._ptr(case.v), nvb._ptr(out),
-           nvb._ptr(case.cu_q), nvb._ptr(case.kv_lens), nvb._ptr(case.block_table), BATCH, BATCH, 1, CTX, QH, KVH,
+           nvb._ptr(case.cu_q), nvb._ptr(case.kv_lens), nvb._ptr(case.block_table), batch, batch, 1, CTX, QH, KVH,
            BS, case.table_stride, splits, nvb._ptr(lse), nvb._ptr(la), nvb._ptr(oa), case.num_blocks]
 
     def step():
@@ -283,63 +287,67 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, launch_ms = t.tolist()
     ms_per_step = ms / args.steps
-    step_bytes = BATCH * bytes_per_seq()
+    step_bytes = batch * bytes_per_seq()
     value = world * step_bytes / (ms_per_step / 1e3) / 1e9
     achieved = step_bytes / (launch_ms / 1e3) / 1e9
     assert nvb.device_error() == 0, "device pipeline wait timed out"
 
     # ---------------- end to end through the public API, host buffers
-    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
-    g = torch.Generator(device=dev).manual_seed(100 + rank)
-    qkv_h = pin(torch.randn(BATCH, QH + 2 * KVH, DIM, generator=g, device=dev).bfloat16())
-    qw = (1 + 0.02 * torch.randn(DIM, generator=g, device=dev)).bfloat16()
-    kw = (1 + 0.02 * torch.randn(DIM, generator=g, device=dev)).bfloat16()
-    positions_h = pin((case.kv_lens - 1).to(torch.int32))
-    table_cpu = case.block_table.cpu()
-    slots_h = pin(torch.tensor([int(table_cpu[i, (CTX - 1) // BS]) * BS + (CTX - 1) % BS for i in range(BATCH)],
-                               dtype=torch.int32))
-    table_h, lens_h, cuq_h = pin(case.block_table), pin(case.kv_lens), pin(case.cu_q)
-    out_h = torch.empty(BATCH, QH, DIM, dtype=torch.bfloat16).pin_memory()
-    dev_in = {n: torch.empty_like(t, device=dev) for n, t in
-              (("qkv", qkv_h), ("pos", positions_h), ("slots", slots_h), ("table", table_h), ("lens", lens_h),
-               ("cuq", cuq_h))}
-    host_in = {"qkv": qkv_h, "pos": positions_h, "slots": slots_h, "table": table_h, "lens": lens_h, "cuq": cuq_h}
-    rope = torch.empty(CTX, DIM, dtype=torch.float32, device=dev)
-    nvb.rope_cache(rope, CTX, DIM, 1e6)
-    q_dev = torch.empty(BATCH, QH, DIM, dtype=torch.bfloat16, device=dev)
-    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
-    d2h = out_h.numel() * out_h.element_size()
+    e2e_value = e2e_ms = None
+    h2d = d2h = 0
+    e2e_steps = 1
+    if not args.no_e2e:
+        pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        qkv_h = pin(torch.randn(batch, QH + 2 * KVH, DIM, generator=g, device=dev).bfloat16())
+        qw = (1 + 0.02 * torch.randn(DIM, generator=g, device=dev)).bfloat16()
+        kw = (1 + 0.02 * torch.randn(DIM, generator=g, device=dev)).bfloat16()
+        positions_h = pin((case.kv_lens - 1).to(torch.int32))
+        table_cpu = case.block_table.cpu()
+        slots_h = pin(torch.tensor([int(table_cpu[i, (CTX - 1) // BS]) * BS + (CTX - 1) % BS for i in range(batch)],
+                                   dtype=torch.int32))
+        table_h, lens_h, cuq_h = pin(case.block_table), pin(case.kv_lens), pin(case.cu_q)
+        out_h = torch.empty(batch, QH, DIM, dtype=torch.bfloat16).pin_memory()
+        dev_in = {n: torch.empty_like(t, device=dev) for n, t in
+                  (("qkv", qkv_h), ("pos", positions_h), ("slots", slots_h), ("table", table_h), ("lens", lens_h),
+                   ("cuq", cuq_h))}
+        host_in = {"qkv": qkv_h, "pos": positions_h, "slots": slots_h, "table": table_h, "lens": lens_h, "cuq": cuq_h}
+        rope = torch.empty(CTX, DIM, dtype=torch.float32, device=dev)
+        nvb.rope_cache(rope, CTX, DIM, 1e6)
+        q_dev = torch.empty(batch, QH, DIM, dtype=torch.bfloat16, device=dev)
+        h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+        d2h = out_h.numel() * out_h.element_size()
 
-    def e2e_step():
-        for n, t in host_in.items():
-            dev_in[n].copy_(t, non_blocking=True)
-        nvb.qkv_rope_cached(dev_in["qkv"], qw, kw, dev_in["pos"], dev_in["slots"], q_dev, case.k, case.v, rows=BATCH,
-                            q_heads=QH, kv_heads=KVH, head_dim=DIM, block_size=BS, num_blocks=case.num_blocks,
-                            eps=1e-6, rope_cache=rope, max_positions=CTX)
-        nvb.paged_fwd(q_dev, case.k, case.v, out, dev_in["cuq"], dev_in["lens"], dev_in["table"], batch=BATCH,
-                      max_q=1, max_k=CTX, q_heads=QH, kv_heads=KVH, block_size=BS, table_stride=case.table_stride,
-                      num_blocks=case.num_blocks, num_splits=splits, lse=lse, lse_accum=la, out_accum=oa)
-        out_h.copy_(out, non_blocking=True)
+        def e2e_step():
+            for n, t in host_in.items():
+                dev_in[n].copy_(t, non_blocking=True)
+            nvb.qkv_rope_cached(dev_in["qkv"], qw, kw, dev_in["pos"], dev_in["slots"], q_dev, case.k, case.v, rows=batch,
+                                q_heads=QH, kv_heads=KVH, head_dim=DIM, block_size=BS, num_blocks=case.num_blocks,
+                                eps=1e-6, rope_cache=rope, max_positions=CTX)
+            nvb.paged_fwd(q_dev, case.k, case.v, out, dev_in["cuq"], dev_in["lens"], dev_in["table"], batch=batch,
+                          max_q=1, max_k=CTX, q_heads=QH, kv_heads=KVH, block_size=BS, table_stride=case.table_stride,
+                          num_blocks=case.num_blocks, num_splits=splits, lse=lse, lse_accum=la, out_accum=oa)
+            out_h.copy_(out, non_blocking=True)
 
-    e2e_steps = max(10, min(args.steps, 200))
-    for _ in range(3):
-        e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = t.item()
-    e2e_value = world * step_bytes / (e2e_ms / e2e_steps / 1e3) / 1e9
-    del qkv_h, dev_in
+        e2e_steps = max(10, min(args.steps, 200))
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = t.item()
+        e2e_value = world * step_bytes / (e2e_ms / e2e_steps / 1e3) / 1e9
+        del qkv_h, dev_in
 
     # ---------------- prefill TFLOP/s (config 2), rank-local
     prefill = None
@@ -391,7 +399,8 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": BATCH * world, "seq_len": CTX,
+            "config": {"workload": WORKLOAD if batch == BATCH else WORKLOAD.replace("256 sequences", f"{batch} sequences"),
+                       "global_batch": batch * world, "seq_len": CTX,
                        "parallelism": f"dp{world} (independent sequence shards, no collective)",
                        "l2": "no flush: 4.3 GB of KV per GPU >> 126 MB L2", "num_splits": splits},
             "pct_peak": round(100 * value / world / hbm_peak, 2),
@@ -400,12 +409,13 @@ def main():
                          "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
                          "kernel": "decode_kernel", "algorithmic_bytes_per_launch": step_bytes,
                          "launch_ms": round(launch_ms, 5)},
-            "tok_s": round(world * BATCH / (ms_per_step / 1e3), 1),
+            "tok_s": round(world * batch / (ms_per_step / 1e3), 1),
             "tok_s_note": "decode query tokens per second through one attention layer",
             "prefill": prefill,
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": round(e2e_ms / e2e_steps, 5),
-                    "path": "pinned H2D of step inputs -> nvb_qkv_rope_cached -> nvb_paged_fwd_ex -> D2H output"},
+            "e2e": None if e2e_value is None else {
+                "value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms / e2e_steps, 5),
+                "path": "pinned H2D of step inputs -> nvb_qkv_rope_cached -> nvb_paged_fwd_ex -> D2H output"},
             "gpu_launches": args.steps * (1 if splits == 1 else 2),
             "clocks": clock_rec,
             "cpu_baseline": cpu,

@@ -452,9 +452,8 @@ cudaError_t launch_gc(const DecodeParams& p, const CUtensorMap& kmap, const CUte
 
 }  // namespace decode_detail
 
-using namespace decode_detail;
-
 int decode_group_chunk(int group) {
+  using namespace decode_detail;
   // Heads of one GQA group processed by one CTA: the largest divisor <= 8.
   for (int gc = 8; gc >= 1; --gc)
     if (group % gc == 0) return gc;
@@ -463,6 +462,7 @@ int decode_group_chunk(int group) {
 
 cudaError_t launch_decode(DecodeParams p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                           cudaStream_t stream) {
+  using namespace decode_detail;
   const int group = p.qh / p.kvh;
   const int gc = decode_group_chunk(group);
   p.n_hgroups = group / gc;

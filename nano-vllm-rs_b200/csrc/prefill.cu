@@ -1,12 +1,490 @@
-// Varlen / chunked causal prefill over paged KV on tcgen05 tensor cores.
+// Varlen / chunked causal prefill over the paged KV cache on tcgen05 tensor
+// cores (sm_100a).
+//
+// Replaces the reference's prefill paths: FA2's paged split-KV kernel with
+// num_splits = 1 and a bottom-right causal mask (SM80 mma.sync, launched from
+// kernels/flash_native/flash_native.cu:102-112) and the native ordered kernel
+// (kernels/kernels.cu:288-354, one CTA per query row). The causal rule is the
+// reference's: query i of a q_len-query group sees keys
+// [0, kv_len - q_len + i] (src/model.rs:1170-1188, smoke.cu:58).
+//
+// One CTA handles one 128-row query tile of one (sequence, kv head). Rows pack
+// the GQA group: row r = (query q0 + r / G, head h*G + r % G), so each K/V
+// tile loaded from HBM serves all G query heads. Per 128-key KV tile j:
+//
+//   S_j = Q K_j^T   tcgen05.mma kind::f16, M=128 N=128 K=128 (8 x K16), A and
+//                   B from 128B-swizzled shared memory, D in TMEM (FP32)
+//   P_j = exp2(S_j * scale*log2e - m)   4 softmax warps, one TMEM lane (row)
+//                   per thread, written to swizzled shared memory as BF16
+//   O  += P_j V_j   tcgen05.mma, V as an MN-major B operand, O in TMEM
+//
+// Warp roles: warp 0 issues TMA (Q once, then a 2-stage K ring and a 2-stage V
+// ring over the sequence's pages: 3-D tensor maps over [tokens, kv_heads,
+// 128] with 64-element, 128-byte-swizzled boxes; a 128-key tile never crosses
+// a page since block_size is a multiple of 256); warp 1 owns TMEM (512
+// columns: S double buffer at 0 and 128, O at 256) and one thread issues the
+// MMAs and tcgen05.commit arrivals; warps 2..5 run the online softmax, the O
+// rescale (TMEM ld/st) and the epilogue. S is double-buffered so the MMA of
+// S_{j+1} overlaps the softmax of S_j, and PV_{j-1} overlaps it as well.
+//
+// Every wait is bounded (common.cuh); a timeout records an error code and the
+// CTA still frees its TMEM and exits.
 #include "internal.cuh"
 
 namespace nvb {
 
+namespace prefill_detail {
+
+constexpr int kRows = 128;
+constexpr int kKeys = 128;
+constexpr int kStages = 2;
+constexpr int kHalfBytes = kRows * 128;    // 128 rows x 64 BF16 (one 128-byte swizzle column)
+constexpr int kTileBytes = 2 * kHalfBytes;  // 128 x 128 BF16
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr int kOCol = 256;
+constexpr float kLn2 = 0.693147180559945309f;
+
+constexpr int kQOff = 0;
+constexpr int kKOff = kQOff + kTileBytes;
+constexpr int kVOff = kKOff + kStages * kTileBytes;
+constexpr int kPOff = kVOff + kStages * kTileBytes;
+constexpr int kBarOff = kPOff + kTileBytes;
+enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kSFree = 11, kPFull = 13,
+           kODone = 14, kNumBars = 15 };
+constexpr int kTmemSlotOff = kBarOff + 16 * 8;
+constexpr int kSmemBytes = kTmemSlotOff + 16 + 1024;  // + alignment slack
+
+struct PrefillParams {
+  const int* cu_q;
+  const int* kv_lens;
+  const int* block_table;
+  __nv_bfloat16* out;
+  float* lse;
+  int batch, max_q, qh, kvh, group, qt, rows_used, block_size, table_stride, num_blocks;
+  float scale_log2;
+};
+
+// ------------------------------------------------------------- tcgen05 PTX
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 format: start
+// address >> 4 in bits 0-13, leading byte offset >> 4 in 16-29, stride byte
+// offset >> 4 in 32-45, version 1 in bits 46-47, layout type 2 in 61-63).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
+         (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+// Instruction descriptor, kind::f16: FP32 accumulator, BF16 A and B, A
+// K-major, B K-major (S = Q K^T) or MN-major (O += P V), M = 128, N = 128.
+constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescPV = kIdescS | (1u << 16);
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+#define NVB_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), \
+                  "=r"(r[i + 6]), "=r"(r[i + 7])
+#define NVB_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), \
+                  "r"(r[i + 6]), "r"(r[i + 7])
+
+// 32 consecutive FP32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : NVB_R8(0), NVB_R8(8), NVB_R8(16), NVB_R8(24)
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      NVB_W8(0), NVB_W8(8), NVB_W8(16), NVB_W8(24)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void st_shared_zero16(uint32_t addr) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0) : "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ bool page_ok(int page, int num_blocks) { return page >= 0 && page < num_blocks; }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
+                   const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ unsigned char smem_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms.
+  const uint32_t raw_addr = smem_addr(smem_raw);
+  unsigned char* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  const uint32_t sbase = smem_addr(smem);
+
+  const int tile = gridDim.x - 1 - blockIdx.x;  // longest causal tiles first
+  const int b = blockIdx.y, h = blockIdx.z;
+  const int q_begin = p.cu_q[b];
+  const int q_len = p.cu_q[b + 1] - q_begin;
+  const int q0 = tile * p.qt;
+  if (q0 >= q_len) return;
+  const int kv_len = p.kv_lens[b];
+  const int qt_eff = min(p.qt, q_len - q0);
+  const int prefix = kv_len - q_len;  // keys before this sequence's first query
+  const int key_end = min(kv_len, prefix + q0 + qt_eff);
+  const int n_tiles = key_end > 0 ? (key_end + kKeys - 1) / kKeys : 0;
+  const int free_keys = min(kv_len, prefix + q0 + 1);  // keys every row of the tile sees
+  const int full_tiles = free_keys > 0 ? free_keys / kKeys : 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int* table = p.block_table + (long long)b * p.table_stride;
+
+  if (n_tiles == 0) {
+    // No visible keys (kv_len < q_len is invalid input): zero rows, -inf LSE.
+    for (int e = threadIdx.x; e < p.rows_used * 128; e += blockDim.x) {
+      const int r = e >> 7, d = e & 127, rq = r / p.group;
+      if (rq >= qt_eff) continue;
+      const long long tok = (long long)q_begin + q0 + rq;
+      const int head = h * p.group + r % p.group;
+      p.out[(tok * p.qh + head) * 128 + d] = __float2bfloat16_rn(0.0f);
+      if (d == 0 && p.lse) p.lse[((long long)b * p.qh + head) * p.max_q + q0 + rq] = -INFINITY;
+    }
+    return;
+  }
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTmemSlotOff);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[kQFull], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars[kKFull + s], 1);
+      mbar_init(&bars[kKEmpty + s], 1);
+      mbar_init(&bars[kVFull + s], 1);
+      mbar_init(&bars[kVEmpty + s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[kSFull + s], 1);
+      mbar_init(&bars[kSFree + s], 4);
+    }
+    mbar_init(&bars[kPFull], 4);
+    mbar_init(&bars[kODone], 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (warp >= 2 && p.rows_used < kRows) {
+    // Rows past the packed (query, head) rows are not loaded: zero them.
+    const int t = threadIdx.x - 64;
+    for (int e = t; e < (kRows - p.rows_used) * 16; e += 128) {
+      const int r = p.rows_used + (e >> 4), c = e & 15;
+      st_shared_zero16(sbase + kQOff + (c >> 3) * kHalfBytes + r * 128 + (c & 7) * 16);
+    }
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // -------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&qmap);
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+      mbar_arrive_expect_tx(&bars[kQFull], 2u * 128u * uint32_t(p.rows_used));
+      const int qy = h * p.group, qz = q_begin + q0;
+      tma_load_3d(smem + kQOff, &qmap, &bars[kQFull], 0, qy, qz);
+      tma_load_3d(smem + kQOff + kHalfBytes, &qmap, &bars[kQFull], 64, qy, qz);
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j % kStages;
+        const uint32_t par = ((j / kStages) + 1) & 1;
+        const int key0 = j * kKeys;
+        const int logical = key0 / p.block_size;
+        const int page = table[logical];
+        const bool ok = page_ok(page, p.num_blocks);
+        const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
+        if (j >= kStages && !mbar_wait(&bars[kKEmpty + st], par, kErrPrefillWait)) break;
+        unsigned char* kdst = smem + kKOff + st * kTileBytes;
+        if (ok) {
+          mbar_arrive_expect_tx(&bars[kKFull + st], kTileBytes);
+          tma_load_3d(kdst, &kmap, &bars[kKFull + st], 0, h, trow);
+          tma_load_3d(kdst + kHalfBytes, &kmap, &bars[kKFull + st], 64, h, trow);
+        } else {
+          mbar_arrive(&bars[kKFull + st]);
+        }
+        if (j >= kStages && !mbar_wait(&bars[kVEmpty + st], par, kErrPrefillWait)) break;
+        unsigned char* vdst = smem + kVOff + st * kTileBytes;
+        if (ok) {
+          mbar_arrive_expect_tx(&bars[kVFull + st], kTileBytes);
+          tma_load_3d(vdst, &vmap, &bars[kVFull + st], 0, h, trow);
+          tma_load_3d(vdst + kHalfBytes, &vmap, &bars[kVFull + st], 64, h, trow);
+        } else {
+          mbar_arrive(&bars[kVFull + st]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool alive = mbar_wait(&bars[kQFull], 0, kErrPrefillWait);
+      tc_fence_after();
+      const uint32_t q_addr = sbase + kQOff, p_addr = sbase + kPOff;
+      auto issue_pv = [&](int t) {
+        const int st = t % kStages;
+        alive = alive && mbar_wait(&bars[kPFull], t & 1, kErrPrefillWait);
+        alive = alive && mbar_wait(&bars[kVFull + st], (t / kStages) & 1, kErrPrefillWait);
+        if (!alive) return;
+        tc_fence_after();
+        const uint32_t v_addr = sbase + kVOff + st * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t a = sw128_desc(p_addr + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(v_addr + kk * 2048, kHalfBytes, 1024);
+          umma_bf16(tmem + kOCol, a, bd, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&bars[kVEmpty + st]);
+        umma_commit(&bars[kODone]);
+      };
+      for (int j = 0; j < n_tiles && alive; ++j) {
+        const int st = j % kStages, sb = j & 1;
+        alive = mbar_wait(&bars[kKFull + st], (j / kStages) & 1, kErrPrefillWait);
+        if (alive && j >= 2) alive = mbar_wait(&bars[kSFree + sb], ((j >> 1) + 1) & 1, kErrPrefillWait);
+        if (!alive) break;
+        tc_fence_after();
+        const uint32_t k_addr = sbase + kKOff + st * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          umma_bf16(tmem + sb * kKeys, sw128_desc(q_addr + off, 16, 1024), sw128_desc(k_addr + off, 16, 1024),
+                    kIdescS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars[kKEmpty + st]);
+        umma_commit(&bars[kSFull + sb]);
+        if (j >= 1) issue_pv(j - 1);
+      }
+      if (alive) issue_pv(n_tiles - 1);
+    }
+  } else {
+    // ---------------------------------------------- softmax and epilogue
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // TMEM lane = packed row
+    const uint32_t trow = tmem + (uint32_t(quad * 32) << 16);
+    const int rq = r / p.group;
+    const bool valid_row = r < p.rows_used && rq < qt_eff;
+    const int limit = valid_row ? prefix + q0 + rq : key_end - 1;  // last visible key
+    const float sl2 = p.scale_log2;
+    float m = -INFINITY, l = 0.0f;
+    bool alive = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&bars[kSFull + sb], (j >> 1) & 1, kErrPrefillWait)) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      float s[kKeys];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t raw[32];
+        tmem_ld32(trow + sb * kKeys + c * 32, raw);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kSFree + sb]);
+
+      const int key0 = j * kKeys;
+      const int logical = key0 / p.block_size;
+      const bool ok = page_ok(table[logical], p.num_blocks);
+      if (j >= full_tiles || !ok) {
+        const int lim = ok ? min(limit, kv_len - 1) - key0 : -1;
+#pragma unroll
+        for (int c = 0; c < kKeys; ++c)
+          if (c > lim) s[c] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int c = 1; c < kKeys; ++c) mx = fmaxf(mx, s[c]);
+      const float m_new = fmaxf(m, mx * sl2);
+      const float m_use = m_new == -INFINITY ? 0.0f : m_new;
+      const float alpha = fast_exp2(m - m_use);  // m = -inf gives 0
+      float rowsum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < kKeys; ++c) {
+        s[c] = fast_exp2(fmaf(s[c], sl2, -m_use));
+        rowsum += s[c];
+      }
+      l = l * alpha + rowsum;
+      m = m_new;
+
+      if (j >= 1) {
+        if (!mbar_wait(&bars[kODone], (j - 1) & 1, kErrPrefillWait)) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t raw[32];
+            tmem_ld32(trow + kOCol + c * 32, raw);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(__uint_as_float(raw[i]) * alpha);
+            tmem_st32(trow + kOCol + c * 32, raw);
+          }
+          tmem_st_wait();
+        }
+      }
+      // V rows that are not real keys (past kv_len, or an invalid page) are
+      // zeroed so that P = 0 never meets a non-finite cache value.
+      const int real_keys = ok ? min(kKeys, kv_len - key0) : 0;
+      if (real_keys < kKeys) {
+        const int st = j % kStages;
+        if (!mbar_wait(&bars[kVFull + st], (j / kStages) & 1, kErrPrefillWait)) {
+          alive = false;
+          break;
+        }
+        if (r >= real_keys) {
+          const uint32_t vrow = sbase + kVOff + st * kTileBytes + r * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            st_shared_zero16(vrow + c * 16);
+            st_shared_zero16(vrow + kHalfBytes + c * 16);
+          }
+        }
+      }
+      // P row -> BF16, 128-byte swizzled K-major layout
+      const uint32_t prow = sbase + kPOff + r * 128;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint32_t w0 = pack_bf16x2(s[8 * c + 0], s[8 * c + 1]);
+        const uint32_t w1 = pack_bf16x2(s[8 * c + 2], s[8 * c + 3]);
+        const uint32_t w2 = pack_bf16x2(s[8 * c + 4], s[8 * c + 5]);
+        const uint32_t w3 = pack_bf16x2(s[8 * c + 6], s[8 * c + 7]);
+        const uint32_t chunk = uint32_t((c & 7) ^ (r & 7));
+        st_shared_v4(prow + (c >> 3) * kHalfBytes + chunk * 16, w0, w1, w2, w3);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kPFull]);
+    }
+
+    // epilogue: O / l -> BF16 rows of `out`, natural-log LSE
+    if (alive && mbar_wait(&bars[kODone], (n_tiles - 1) & 1, kErrPrefillWait)) {
+      tc_fence_after();
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+      const int head = h * p.group + (r % p.group);
+      const long long tok = (long long)q_begin + q0 + rq;
+      __nv_bfloat16* dst = p.out + (tok * p.qh + head) * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t raw[32];
+        tmem_ld32(trow + kOCol + c * 32, raw);
+        tmem_ld_wait();
+        if (valid_row) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(raw[8 * v + 0]) * inv, __uint_as_float(raw[8 * v + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(raw[8 * v + 2]) * inv, __uint_as_float(raw[8 * v + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(raw[8 * v + 4]) * inv, __uint_as_float(raw[8 * v + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(raw[8 * v + 6]) * inv, __uint_as_float(raw[8 * v + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = w;
+          }
+        }
+      }
+      if (valid_row && p.lse)
+        p.lse[((long long)b * p.qh + head) * p.max_q + q0 + rq] = l > 0.0f ? (m + fast_log2(l)) * kLn2 : -INFINITY;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+}  // namespace prefill_detail
+
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
-  (void)a;
-  (void)stream;
-  return cudaErrorNotSupported;
+  using namespace prefill_detail;
+  const int group = a.qh / a.kvh;
+  if (group < 1 || group > 16 || a.batch > 65535 || a.kvh > 65535) return cudaErrorNotSupported;
+  const int qt = kRows / group;
+  PrefillParams p{};
+  p.cu_q = a.cu_q;
+  p.kv_lens = a.kv_lens;
+  p.block_table = a.block_table;
+  p.out = static_cast<__nv_bfloat16*>(const_cast<void*>(a.out));
+  p.lse = a.lse;
+  p.batch = a.batch;
+  p.max_q = a.max_q;
+  p.qh = a.qh;
+  p.kvh = a.kvh;
+  p.group = group;
+  p.qt = qt;
+  p.rows_used = qt * group;
+  p.block_size = a.block_size;
+  p.table_stride = a.table_stride;
+  p.num_blocks = a.num_blocks;
+  p.scale_log2 = 1.4426950408889634f / 11.313708498984761f;
+
+  const CUtensorMap *qmap = nullptr, *kmap = nullptr, *vmap = nullptr;
+  {
+    const uint64_t dims[3] = {128, uint64_t(a.qh), uint64_t(a.total_q)};
+    const uint64_t strides[2] = {256, uint64_t(a.qh) * 256};
+    const uint32_t box[3] = {64, uint32_t(group), uint32_t(qt)};
+    if (make_map_3d(a.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, &qmap)) return cudaErrorInvalidValue;
+  }
+  {
+    const uint64_t dims[3] = {128, uint64_t(a.kvh), uint64_t(a.num_blocks) * uint64_t(a.block_size)};
+    const uint64_t strides[2] = {256, uint64_t(a.kvh) * 256};
+    const uint32_t box[3] = {64, 1, 128};
+    if (make_map_3d(a.k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, &kmap)) return cudaErrorInvalidValue;
+    if (make_map_3d(a.v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, &vmap)) return cudaErrorInvalidValue;
+  }
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit)) {
+    e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
+  }
+  const dim3 grid((a.max_q + qt - 1) / qt, a.batch, a.kvh);
+  prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p, *qmap, *kmap, *vmap);
+  return cudaGetLastError();
 }
 
 }  // namespace nvb

@@ -124,12 +124,11 @@ __global__ void rope_cache_kernel(float* cache, int positions, int dim, float th
 
 }  // namespace rope_detail
 
-using namespace rope_detail;
-
 cudaError_t launch_qkv_rope(cudaStream_t stream, bool cached, const void* qkv, const void* qw,
                             const void* kw, const int* positions, const int* slots, void* qout,
                             void* kc, void* vc, int rows, int qh, int kvh, int bs, int blocks,
                             float eps, float theta, const float* rope_cache, int max_positions) {
+  using namespace rope_detail;
   const long long items = (long long)rows * (qh + kvh);
   const int warps_per_block = 8;
   const long long grid = (items + warps_per_block - 1) / warps_per_block;
@@ -151,6 +150,7 @@ cudaError_t launch_qkv_rope(cudaStream_t stream, bool cached, const void* qkv, c
 }
 
 cudaError_t launch_rope_cache(cudaStream_t stream, float* cache, int positions, int dim, float theta) {
+  using namespace rope_detail;
   const long long elements = (long long)positions * (dim / 2);
   long long grid = (elements + 255) / 256;
   if (grid > 65535) grid = 65535;

@@ -67,8 +67,8 @@ class RefNative:
         L.nv_destroy.argtypes = [P]
         L.nv_destroy.restype = None
         L.nv_last_error.restype = ctypes.c_char_p
-        L.nv_attention.argtypes = [P] * 8 + [I] * 10
-        L.nv_attention_splitkv_candidate.argtypes = [P] * 8 + [I] * 10 + [P, I]
+        L.nv_attention.argtypes = [P] * 8 + [I] * 9
+        L.nv_attention_splitkv_candidate.argtypes = [P] * 8 + [I] * 9 + [P, I]
         L.nv_qkv_rope_cached.argtypes = [P] * 9 + [I] * 6 + [F, P, I]
         L.nv_qkv_rope.argtypes = [P] * 9 + [I] * 6 + [F, F]
         L.nv_rope_cache.argtypes = [P, P, I, I, F]

@@ -28,8 +28,12 @@ def _inputs(rows, seed):
     positions = torch.randint(0, MAXPOS, (rows,), generator=gc, dtype=torch.int32)
     slots = torch.randperm(BS * BLOCKS, generator=gc)[:rows].to(torch.int32)
     # edge cases: out-of-range positions (cos 1, sin 0) and skipped slots
-    positions[0], positions[1], positions[2], positions[3] = 0, MAXPOS - 1, -5, MAXPOS + 7
-    slots[4], slots[5] = -1, BS * BLOCKS
+    for i, val in enumerate((0, MAXPOS - 1, -5, MAXPOS + 7)):
+        if i < rows:
+            positions[i] = val
+    for i, val in ((4, -1), (5, BS * BLOCKS)):
+        if i < rows:
+            slots[i] = val
     return qkv, qw, kw, positions.cuda(), slots.cuda()
 
 
