@@ -149,7 +149,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kv_len = p.kv_lens[b];
   const int qt_eff = min(p.qt, q_len - q0);
   const int prefix = kv_len - q_len;  // keys before this sequence's first query
-  const int key_end = min(kv_len, prefix + q0 + qt_eff);
+  // A context longer than the page table, or shorter than its query group,
+  // is invalid input: such rows get zero output (as decode does).
+  const bool seq_ok = prefix >= 0 && (long long)kv_len <= (long long)p.table_stride * p.block_size;
+  const int key_end = seq_ok ? min(kv_len, prefix + q0 + qt_eff) : 0;
   const int n_tiles = key_end > 0 ? (key_end + kKeys - 1) / kKeys : 0;
   const int free_keys = min(kv_len, prefix + q0 + 1);  // keys every row of the tile sees
   const int full_tiles = free_keys > 0 ? free_keys / kKeys : 0;
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int* table = p.block_table + (long long)b * p.table_stride;
 
   if (n_tiles == 0) {
-    // No visible keys (kv_len < q_len is invalid input): zero rows, -inf LSE.
+    // No visible keys (invalid context): zero rows, -inf LSE.
     for (int e = threadIdx.x; e < p.rows_used * 128; e += blockDim.x) {
       const int r = e >> 7, d = e & 127, rq = r / p.group;
       if (rq >= qt_eff) continue;

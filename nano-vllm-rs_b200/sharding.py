@@ -1,0 +1,100 @@
+"""Multi-GPU decode sharding for the paged attention path.
+
+Two partitions of the work, one process per GPU over torch.distributed:
+
+* by sequence (configuration 3, engine replicas of configuration 4): each
+  rank decodes its own sequences against its own cache; there is no
+  collective on the data path (`sequence_shard`).
+* by kv head (configuration 5, long context): rank r owns kv heads
+  [r*kvh_local, (r+1)*kvh_local) of every sequence and the query heads of
+  their GQA groups; its cache holds only those kv heads. Each rank runs the
+  split-KV decode on its heads, then one all-gather of the BF16 outputs
+  rebuilds [batch, q_heads, 128] on every rank (`KvHeadShardedDecode`).
+  The transfer is batch * q_heads * 256 B (8 KiB per rank at 4 x 64 heads),
+  so NCCL over NVLink is launch-latency bound; no kernel reads peer memory.
+
+The reference is single-GPU (its README: no NCCL, MPI or tensor
+parallelism); this module is the B200 build's own.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+
+@dataclass(frozen=True)
+class HeadShard:
+    rank: int
+    world: int
+    kv_heads: int          # total kv heads
+    q_heads: int           # total query heads
+
+    def __post_init__(self):
+        if self.kv_heads % self.world or self.q_heads % self.kv_heads:
+            raise ValueError(f"{self.kv_heads} kv heads / {self.q_heads} q heads do not shard over {self.world} ranks")
+
+    @property
+    def kv_local(self) -> int:
+        return self.kv_heads // self.world
+
+    @property
+    def q_local(self) -> int:
+        return self.q_heads // self.world
+
+    @property
+    def kv_range(self):
+        return range(self.rank * self.kv_local, (self.rank + 1) * self.kv_local)
+
+    @property
+    def q_range(self):
+        return range(self.rank * self.q_local, (self.rank + 1) * self.q_local)
+
+
+def sequence_shard(batch: int, rank: int, world: int):
+    """Contiguous sequence range of `rank` (sizes differ by at most one)."""
+    base, extra = divmod(batch, world)
+    start = rank * base + min(rank, extra)
+    return range(start, start + base + (1 if rank < extra else 0))
+
+
+def gather_heads(local_out, shard: HeadShard, group=None):
+    """All-gathers per-rank outputs [batch, q_local, D] into [batch, q_heads, D]
+    with query heads in global order."""
+    import torch
+    import torch.distributed as dist
+
+    b, ql, d = local_out.shape
+    buf = torch.empty(shard.world * b * ql * d, dtype=local_out.dtype, device=local_out.device)
+    dist.all_gather_into_tensor(buf, local_out.contiguous().view(-1), group=group)
+    return buf.view(shard.world, b, ql, d).permute(1, 0, 2, 3).reshape(b, shard.world * ql, d)
+
+
+class KvHeadShardedDecode:
+    """Decode over a kv-head-sharded paged cache followed by an NCCL
+    all-gather. `k_local` / `v_local` are this rank's caches
+    [num_blocks, block_size, kv_local, 128]; `q_local` is
+    [batch, q_local, 128] (the query heads of this rank's kv heads)."""
+
+    def __init__(self, nvb, shard: HeadShard, *, batch, block_size, table_stride, num_blocks, max_k, device,
+                 num_splits=None, group=None):
+        import torch
+
+        self.nvb, self.shard, self.group = nvb, shard, group
+        self.batch, self.block_size, self.table_stride = batch, block_size, table_stride
+        self.num_blocks, self.max_k = num_blocks, max_k
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        self.splits = num_splits or nvb.num_splits(batch, shard.q_local, shard.kv_local, max_k, sms)
+        self.out_local = torch.empty(batch, shard.q_local, 128, dtype=torch.bfloat16, device=device)
+        self.lse = torch.empty(batch, shard.q_local, 1, dtype=torch.float32, device=device)
+        self.la, self.oa = (nvb.splitkv_scratch(self.splits, batch, shard.q_local, device) if self.splits > 1
+                            else (None, None))
+
+    def local(self, q_local, k_local, v_local, cu_q, kv_lens, block_table, check=True):
+        self.nvb.paged_fwd(q_local, k_local, v_local, self.out_local, cu_q, kv_lens, block_table, batch=self.batch,
+                           max_q=1, max_k=self.max_k, q_heads=self.shard.q_local, kv_heads=self.shard.kv_local,
+                           block_size=self.block_size, table_stride=self.table_stride, num_blocks=self.num_blocks,
+                           num_splits=self.splits, lse=self.lse, lse_accum=self.la, out_accum=self.oa, check=check)
+        return self.out_local
+
+    def __call__(self, q_local, k_local, v_local, cu_q, kv_lens, block_table, check=True):
+        self.local(q_local, k_local, v_local, cu_q, kv_lens, block_table, check)
+        return gather_heads(self.out_local, self.shard, self.group)
