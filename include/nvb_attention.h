@@ -6,10 +6,12 @@
  * Every pointer except `stream` is a CUDA device pointer on the current
  * device. `stream` is a cudaStream_t owned by the caller. No entry point
  * allocates device memory, synchronizes the stream, or owns a context, so
- * all launches are safe inside CUDA-graph stream capture, with one
- * exception: the first launch that sees a new KV-cache base pointer encodes
- * its TMA descriptor on the host (no device work); do that first launch
- * before capture, as the reference engine does with its warm-up forward.
+ * the launches of the entry points below (nvb_paged_decode_static_scratch
+ * aside: see its own comment) are safe inside CUDA-graph stream capture,
+ * with one exception: the first launch that sees a new KV-cache base pointer
+ * encodes its TMA descriptor on the host (no device work); do that first
+ * launch before capture, as the reference engine does with its warm-up
+ * forward.
  *
  * Layouts (identical to the reference):
  *   q, out           [total_q, q_heads, 128] bf16, contiguous
@@ -75,6 +77,22 @@ int nvb_paged_fwd_ex(void* stream, const void* q, const void* k, const void* v, 
                      int total_q, int max_q, int max_k, int q_heads, int kv_heads,
                      int block_size, int table_stride, int num_splits, float* lse,
                      float* lse_accum, float* out_accum, int num_blocks);
+
+/* Split-KV decode that allocates nothing, for callers that cannot call
+ * cudaMalloc (a plugin inside a host process that owns the CUDA allocator, a
+ * fixed device-memory budget): the split partials live in a fixed array in
+ * this library's device memory instead of caller-provided lse_accum /
+ * out_accum. No counterpart in the reference. Decode only (one query per
+ * sequence, total_q == batch); other arguments as nvb_paged_fwd_ex.
+ * Limit: num_splits * batch * q_heads <= 16384 (about 8.1 MB held per GPU
+ * until exit); larger calls return -1. All calls on a device share the array,
+ * so calls that overlap on the GPU race; the first call on each device looks
+ * up the array's address and should come before any stream capture. */
+int nvb_paged_decode_static_scratch(void* stream, const void* q, const void* k, const void* v,
+                                    void* out, const int* cu_q, const int* kv_lens,
+                                    const int* block_table, int batch, int max_k, int q_heads,
+                                    int kv_heads, int block_size, int table_stride,
+                                    int num_splits, float* lse, int num_blocks);
 
 /* Split count for decode, replacing `nvr_flash_num_splits`
  * (kernels/flash_native/flash_native.h:31-32, flash_native.cu:17-38).

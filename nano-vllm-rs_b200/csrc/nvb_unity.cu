@@ -3,3 +3,4 @@
 #include "decode.cu"
 #include "prefill.cu"
 #include "qkv_rope.cu"
+#include "static_scratch.cu"
