@@ -208,6 +208,52 @@ def run_reference(args, rank, world):
     return 0
 
 
+def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
+    """Qwen3-32B attention shape (64q/8kv), 4 sequences of
+    ctx 32768. At N GPUs each rank owns 8/N kv heads (and their query heads),
+    runs split-KV decode on its shard and all-gathers the BF16 outputs over
+    NCCL. Returns whole-job GB/s of algorithmic bytes, timed with CUDA events
+    (max over ranks)."""
+    import importlib
+
+    import torch
+    import torch.distributed as dist
+
+    S = importlib.import_module("nano_vllm_rs_b200.sharding")
+    batch, ctx, qh, kvh = 4, 32768, 64, 8
+    shard = S.HeadShard(rank, world, kv_heads=kvh, q_heads=qh)
+    case = W.paged_case([ctx] * batch, q_heads=shard.q_local, kv_heads=shard.kv_local, seed=500 + rank, device=dev)
+    run = S.KvHeadShardedDecode(nvb, shard, batch=batch, block_size=256, table_stride=case.table_stride,
+                                num_blocks=case.num_blocks, max_k=ctx, device=dev)
+
+    def once():
+        if world > 1:
+            return run(case.q, case.k, case.v, case.cu_q, case.kv_lens, case.block_table, check=False)
+        return run.local(case.q, case.k, case.v, case.cu_q, case.kv_lens, case.block_table, check=False)
+
+    for _ in range(5):
+        once()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        once()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    total_bytes = batch * ctx * kvh * 512 + 2 * batch * qh * 128 * 2
+    return {"value": round(total_bytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 5),
+            "splits_per_gpu": run.splits, "kv_heads_per_gpu": shard.kv_local,
+            "collective": "NCCL all-gather of BF16 outputs" if world > 1 else None,
+            "workload": "config5: 4 seqs x ctx 32768, 64q/8kv, kv-head sharded over the GPUs, split-KV per GPU"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -217,6 +263,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-long-context", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 256 = config 3; smaller only for profiler captures)")
     args = ap.parse_args()
@@ -267,21 +314,20 @@ def main():
     clocks = ClockSampler(local)
     clocks.start()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # per-launch events on a subset of steps give the kernel's own duration
-    probe = min(20, args.steps)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(probe)]
+    # an event pair around every launch gives the kernels' own durations
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     t_start.record(stream)
     for i in range(args.steps):
-        if i < probe:
-            ev[i][0].record(stream)
+        ev[i][0].record(stream)
         step()
-        if i < probe:
-            ev[i][1].record(stream)
+        ev[i][1].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize()
     clock_rec = clocks.stop()
     ms = t_start.elapsed_time(t_end)
-    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    launch_times = [a.elapsed_time(b) for a, b in ev]
+    launch_ms = statistics.mean(launch_times)
+    launch_first, launch_last = statistics.mean(launch_times[:10]), statistics.mean(launch_times[-10:])
     if world > 1:
         t = torch.tensor([ms, launch_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -385,6 +431,11 @@ def main():
                    "workload": "config2: varlen causal prefill, 32 prompts L~U[64,2048] (seed = rank), 16q/8kv, "
                                "FLOPs = 4*128*qh per visible (query, key)"}
 
+    # ---------------- long-context decode (config 5), kv-head sharded for N > 1
+    long_ctx = None
+    if not args.no_long_context and 8 % world == 0:
+        long_ctx = long_context_leg(nvb, W, dev, rank, world, stream)
+
     # ---------------- CPU baseline (rank 0, N = 1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -408,15 +459,18 @@ def main():
                          "frac": round(achieved / hbm_peak, 4), "traffic": profile_traffic(),
                          "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
                          "kernel": "decode_kernel", "algorithmic_bytes_per_launch": step_bytes,
-                         "launch_ms": round(launch_ms, 5)},
+                         "launch_ms": round(launch_ms, 5), "launch_ms_first10": round(launch_first, 5),
+                         "launch_ms_last10": round(launch_last, 5)},
             "tok_s": round(world * batch / (ms_per_step / 1e3), 1),
             "tok_s_note": "decode query tokens per second through one attention layer",
             "prefill": prefill,
+            "long_context": long_ctx,
             "e2e": None if e2e_value is None else {
                 "value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms / e2e_steps, 5),
                 "path": "pinned H2D of step inputs -> nvb_qkv_rope_cached -> nvb_paged_fwd_ex -> D2H output"},
             "gpu_launches": args.steps * (1 if splits == 1 else 2),
+            "gpu_launches_note": "decode_kernel launches (+ combine_kernel when num_splits > 1) in the timed region",
             "clocks": clock_rec,
             "cpu_baseline": cpu,
         }

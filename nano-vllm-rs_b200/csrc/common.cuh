@@ -28,6 +28,7 @@ enum DeviceError : int {
   kErrPrefillWait = 3,        // a prefill pipeline wait gave up
   kErrPrefillTmem = 4,        // TMEM allocation returned an unusable address
   kErrBadPage = 5,            // reserved: a page id outside [0, num_blocks)
+  kErrPrefillAlign = 6,       // prefill: dynamic shared memory base not usable for the tile layout
 };
 
 constexpr long long kWaitCycles = 4000000000LL;

@@ -10,22 +10,31 @@
 //
 // One CTA handles one 128-row query tile of one (sequence, kv head). Rows pack
 // the GQA group: row r = (query q0 + r / G, head h*G + r % G), so each K/V
-// tile loaded from HBM serves all G query heads. Per 128-key KV tile j:
+// tile loaded from HBM serves all G query heads. Per 64-key KV tile j:
 //
-//   S_j = Q K_j^T   tcgen05.mma kind::f16, M=128 N=128 K=128 (8 x K16), A and
+//   S_j = Q K_j^T   tcgen05.mma kind::f16, M=128 N=64 K=128 (8 x K16), A and
 //                   B from 128B-swizzled shared memory, D in TMEM (FP32)
 //   P_j = exp2(S_j * scale*log2e - m)   4 softmax warps, one TMEM lane (row)
 //                   per thread, written to swizzled shared memory as BF16
-//   O  += P_j V_j   tcgen05.mma, V as an MN-major B operand, O in TMEM
+//   O  += P_j V_j   tcgen05.mma M=128 N=128 K=64, V as an MN-major B operand,
+//                   O in TMEM
 //
 // Warp roles: warp 0 issues TMA (Q once, then a 2-stage K ring and a 2-stage V
 // ring over the sequence's pages: 3-D tensor maps over [tokens, kv_heads,
-// 128] with 64-element, 128-byte-swizzled boxes; a 128-key tile never crosses
-// a page since block_size is a multiple of 256); warp 1 owns TMEM (512
-// columns: S double buffer at 0 and 128, O at 256) and one thread issues the
+// 128] with 64-element, 128-byte-swizzled boxes; a 64-key tile never crosses
+// a page since block_size is a multiple of 256); warp 1 owns TMEM (256
+// columns: S double buffer at 0 and 64, O at 128) and one thread issues the
 // MMAs and tcgen05.commit arrivals; warps 2..5 run the online softmax, the O
 // rescale (TMEM ld/st) and the epilogue. S is double-buffered so the MMA of
 // S_{j+1} overlaps the softmax of S_j, and PV_{j-1} overlaps it as well.
+//
+// Sizing for B200: 112 KB of tiles + 1 KB of barriers per CTA and 256 TMEM
+// columns let two CTAs share an SM (2 x 114 KB of the 228 KB, 2 x 256 of the
+// 512 columns), so one CTA's softmax runs while the other's MMAs use the
+// tensor core, and their prologues/epilogues overlap. The softmax keeps the
+// running max it scales by unless a row's max grows by more than 2^8
+// (FA4-style lazy rescale: P stays <= 256, exact after the final divide), so
+// the TMEM read-modify-write of O is rare after the first tiles.
 //
 // Every wait is bounded (common.cuh); a timeout records an error code and the
 // CTA still frees its TMEM and exits.
@@ -36,24 +45,31 @@ namespace nvb {
 namespace prefill_detail {
 
 constexpr int kRows = 128;
-constexpr int kKeys = 128;
+constexpr int kKeys = 64;
 constexpr int kStages = 2;
-constexpr int kHalfBytes = kRows * 128;    // 128 rows x 64 BF16 (one 128-byte swizzle column)
-constexpr int kTileBytes = 2 * kHalfBytes;  // 128 x 128 BF16
+constexpr int kQHalf = kRows * 128;          // 128 rows x 64 BF16 (one 128-byte swizzle column)
+constexpr int kQBytes = 2 * kQHalf;          // Q tile 128 x 128 BF16
+constexpr int kKVHalf = kKeys * 128;         // 64 keys x 64 BF16
+constexpr int kKVBytes = 2 * kKVHalf;        // K or V tile 64 x 128 BF16
+constexpr int kPBytes = kRows * 128;         // P tile 128 x 64 BF16
 constexpr int kThreads = 192;
-constexpr int kTmemCols = 512;
-constexpr int kOCol = 256;
+constexpr int kTmemCols = 256;
+constexpr int kOCol = 128;
 constexpr float kLn2 = 0.693147180559945309f;
+constexpr float kRescaleLog2 = 8.0f;         // lazy rescale threshold (P <= 2^8)
 
-constexpr int kQOff = 0;
-constexpr int kKOff = kQOff + kTileBytes;
-constexpr int kVOff = kKOff + kStages * kTileBytes;
-constexpr int kPOff = kVOff + kStages * kTileBytes;
-constexpr int kBarOff = kPOff + kTileBytes;
+// Barriers and the TMEM slot sit below the first 1024-byte boundary; the
+// tiles follow on 1024-byte boundaries (128-byte swizzle atoms).
 enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kSFree = 11, kPFull = 13,
            kODone = 14, kNumBars = 15 };
-constexpr int kTmemSlotOff = kBarOff + 16 * 8;
-constexpr int kSmemBytes = kTmemSlotOff + 16 + 1024;  // + alignment slack
+constexpr int kTmemSlotOff = kNumBars * 8;
+constexpr int kHeadBytes = kTmemSlotOff + 16;
+constexpr int kQOff = 0;                      // offsets from the aligned tile base
+constexpr int kKOff = kQOff + kQBytes;
+constexpr int kVOff = kKOff + kStages * kKVBytes;
+constexpr int kPOff = kVOff + kStages * kKVBytes;
+constexpr int kTileBytes = kPOff + kPBytes;   // 112 KB
+constexpr int kSmemBytes = 1024 + kTileBytes; // 113 KB: two CTAs per SM
 
 struct PrefillParams {
   const int* cu_q;
@@ -77,10 +93,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uin
          (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 
-// Instruction descriptor, kind::f16: FP32 accumulator, BF16 A and B, A
-// K-major, B K-major (S = Q K^T) or MN-major (O += P V), M = 128, N = 128.
-constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
-constexpr uint32_t kIdescPV = kIdescS | (1u << 16);
+// Instruction descriptors, kind::f16: FP32 accumulator, BF16 A and B, A
+// K-major, M = 128. S = Q K^T: B K-major, N = 64 keys. O += P V: B MN-major,
+// N = 128 head dims.
+constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescS = kIdescBase | ((uint32_t(kKeys) >> 3) << 17);
+constexpr uint32_t kIdescPV = kIdescBase | (1u << 16) | ((128u >> 3) << 17);
 
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
@@ -131,14 +149,15 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 
 __device__ __forceinline__ bool page_ok(int page, int num_blocks) { return page >= 0 && page < num_blocks; }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
                    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
-  extern __shared__ unsigned char smem_raw[];
-  // 1024-byte alignment for the 128-byte swizzle atoms.
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
-  unsigned char* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  const uint32_t sbase = smem_addr(smem);
+  // tiles start at the first 1024-byte boundary past the barrier block
+  const uint32_t tile_addr = (raw_addr + kHeadBytes + 1023u) & ~1023u;
+  unsigned char* tiles = smem_raw + (tile_addr - raw_addr);
+  const uint32_t sbase = tile_addr;
 
   const int tile = gridDim.x - 1 - blockIdx.x;  // longest causal tiles first
   const int b = blockIdx.y, h = blockIdx.z;
@@ -146,6 +165,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q_len = p.cu_q[b + 1] - q_begin;
   const int q0 = tile * p.qt;
   if (q0 >= q_len) return;
+  if (tile_addr + kTileBytes > raw_addr + kSmemBytes) {  // dynamic smem base not 1 KB friendly
+    if (threadIdx.x == 0) record_error(kErrPrefillAlign);
+    return;
+  }
   const int kv_len = p.kv_lens[b];
   const int qt_eff = min(p.qt, q_len - q0);
   const int prefix = kv_len - q_len;  // keys before this sequence's first query
@@ -172,8 +195,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTmemSlotOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + kTmemSlotOff);
 
   if (threadIdx.x == 0) {
     mbar_init(&bars[kQFull], 1);
@@ -202,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = threadIdx.x - 64;
     for (int e = t; e < (kRows - p.rows_used) * 16; e += 128) {
       const int r = p.rows_used + (e >> 4), c = e & 15;
-      st_shared_zero16(sbase + kQOff + (c >> 3) * kHalfBytes + r * 128 + (c & 7) * 16);
+      st_shared_zero16(sbase + kQOff + (c >> 3) * kQHalf + r * 128 + (c & 7) * 16);
     }
     fence_proxy_async_smem();
   }
@@ -219,8 +242,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&vmap);
       mbar_arrive_expect_tx(&bars[kQFull], 2u * 128u * uint32_t(p.rows_used));
       const int qy = h * p.group, qz = q_begin + q0;
-      tma_load_3d(smem + kQOff, &qmap, &bars[kQFull], 0, qy, qz);
-      tma_load_3d(smem + kQOff + kHalfBytes, &qmap, &bars[kQFull], 64, qy, qz);
+      tma_load_3d(tiles + kQOff, &qmap, &bars[kQFull], 0, qy, qz);
+      tma_load_3d(tiles + kQOff + kQHalf, &qmap, &bars[kQFull], 64, qy, qz);
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % kStages;
         const uint32_t par = ((j / kStages) + 1) & 1;
@@ -230,20 +253,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool ok = page_ok(page, p.num_blocks);
         const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
         if (j >= kStages && !mbar_wait(&bars[kKEmpty + st], par, kErrPrefillWait)) break;
-        unsigned char* kdst = smem + kKOff + st * kTileBytes;
+        unsigned char* kdst = tiles + kKOff + st * kKVBytes;
         if (ok) {
-          mbar_arrive_expect_tx(&bars[kKFull + st], kTileBytes);
+          mbar_arrive_expect_tx(&bars[kKFull + st], kKVBytes);
           tma_load_3d(kdst, &kmap, &bars[kKFull + st], 0, h, trow);
-          tma_load_3d(kdst + kHalfBytes, &kmap, &bars[kKFull + st], 64, h, trow);
+          tma_load_3d(kdst + kKVHalf, &kmap, &bars[kKFull + st], 64, h, trow);
         } else {
           mbar_arrive(&bars[kKFull + st]);
         }
         if (j >= kStages && !mbar_wait(&bars[kVEmpty + st], par, kErrPrefillWait)) break;
-        unsigned char* vdst = smem + kVOff + st * kTileBytes;
+        unsigned char* vdst = tiles + kVOff + st * kKVBytes;
         if (ok) {
-          mbar_arrive_expect_tx(&bars[kVFull + st], kTileBytes);
+          mbar_arrive_expect_tx(&bars[kVFull + st], kKVBytes);
           tma_load_3d(vdst, &vmap, &bars[kVFull + st], 0, h, trow);
-          tma_load_3d(vdst + kHalfBytes, &vmap, &bars[kVFull + st], 64, h, trow);
+          tma_load_3d(vdst + kKVHalf, &vmap, &bars[kVFull + st], 64, h, trow);
         } else {
           mbar_arrive(&bars[kVFull + st]);
         }
@@ -261,11 +284,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         alive = alive && mbar_wait(&bars[kVFull + st], (t / kStages) & 1, kErrPrefillWait);
         if (!alive) return;
         tc_fence_after();
-        const uint32_t v_addr = sbase + kVOff + st * kTileBytes;
+        const uint32_t v_addr = sbase + kVOff + st * kKVBytes;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t a = sw128_desc(p_addr + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sw128_desc(v_addr + kk * 2048, kHalfBytes, 1024);
+        for (int kk = 0; kk < kKeys / 16; ++kk) {
+          const uint64_t a = sw128_desc(p_addr + kk * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(v_addr + kk * 2048, kKVHalf, 1024);
           umma_bf16(tmem + kOCol, a, bd, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars[kVEmpty + st]);
@@ -277,11 +300,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (alive && j >= 2) alive = mbar_wait(&bars[kSFree + sb], ((j >> 1) + 1) & 1, kErrPrefillWait);
         if (!alive) break;
         tc_fence_after();
-        const uint32_t k_addr = sbase + kKOff + st * kTileBytes;
+        const uint32_t k_addr = sbase + kKOff + st * kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_bf16(tmem + sb * kKeys, sw128_desc(q_addr + off, 16, 1024), sw128_desc(k_addr + off, 16, 1024),
+          const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
+          const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
+          umma_bf16(tmem + sb * kKeys, sw128_desc(q_addr + qoff, 16, 1024), sw128_desc(k_addr + koff, 16, 1024),
                     kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars[kKEmpty + st]);
@@ -299,51 +323,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool valid_row = r < p.rows_used && rq < qt_eff;
     const int limit = valid_row ? prefix + q0 + rq : key_end - 1;  // last visible key
     const float sl2 = p.scale_log2;
-    float m = -INFINITY, l = 0.0f;
+    float m_used = -INFINITY, l = 0.0f;  // running max the probabilities are scaled by
     bool alive = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int sb = j & 1;
+      const int key0 = j * kKeys;
+      const bool ok = page_ok(table[key0 / p.block_size], p.num_blocks);
       if (!mbar_wait(&bars[kSFull + sb], (j >> 1) & 1, kErrPrefillWait)) {
         alive = false;
         break;
       }
       tc_fence_after();
       float s[kKeys];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t raw[32];
-        tmem_ld32(trow + sb * kKeys + c * 32, raw);
+      {
+        uint32_t raw0[32], raw1[32];
+        tmem_ld32(trow + sb * kKeys, raw0);
+        tmem_ld32(trow + sb * kKeys + 32, raw1);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(raw[i]);
+        for (int i = 0; i < 32; ++i) {
+          s[i] = __uint_as_float(raw0[i]);
+          s[32 + i] = __uint_as_float(raw1[i]);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kSFree + sb]);
 
-      const int key0 = j * kKeys;
-      const int logical = key0 / p.block_size;
-      const bool ok = page_ok(table[logical], p.num_blocks);
       if (j >= full_tiles || !ok) {
         const int lim = ok ? min(limit, kv_len - 1) - key0 : -1;
 #pragma unroll
         for (int c = 0; c < kKeys; ++c)
           if (c > lim) s[c] = -INFINITY;
       }
-      float mx = s[0];
+      float mx8[8];
 #pragma unroll
-      for (int c = 1; c < kKeys; ++c) mx = fmaxf(mx, s[c]);
-      const float m_new = fmaxf(m, mx * sl2);
-      const float m_use = m_new == -INFINITY ? 0.0f : m_new;
-      const float alpha = fast_exp2(m - m_use);  // m = -inf gives 0
-      float rowsum = 0.0f;
+      for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+#pragma unroll
+      for (int c = 8; c < kKeys; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float m_tile = mx * sl2;
+      // Rescale only when the row max grew by more than 2^8 (or on the
+      // first finite max); otherwise keep scaling by the stale max.
+      float alpha = 1.0f;
+      if (m_tile > m_used + kRescaleLog2) {
+        alpha = fast_exp2(m_used - m_tile);  // 0 when m_used = -inf
+        m_used = m_tile;
+      }
+      const float m_exp = m_used == -INFINITY ? 0.0f : m_used;
+      float sum8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sum8[i] = 0.0f;
 #pragma unroll
       for (int c = 0; c < kKeys; ++c) {
-        s[c] = fast_exp2(fmaf(s[c], sl2, -m_use));
-        rowsum += s[c];
+        s[c] = fast_exp2(fmaf(s[c], sl2, -m_exp));
+        sum8[c & 7] += s[c];
       }
-      l = l * alpha + rowsum;
-      m = m_new;
+      l = l * alpha + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
 
       if (j >= 1) {
         if (!mbar_wait(&bars[kODone], (j - 1) & 1, kErrPrefillWait)) {
@@ -351,18 +388,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t raw[32];
-            tmem_ld32(trow + kOCol + c * 32, raw);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) raw[i] = __float_as_uint(__uint_as_float(raw[i]) * alpha);
-            tmem_st32(trow + kOCol + c * 32, raw);
-          }
-          tmem_st_wait();
-        }
       }
       // V rows that are not real keys (past kv_len, or an invalid page) are
       // zeroed so that P = 0 never meets a non-finite cache value.
@@ -373,27 +398,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           alive = false;
           break;
         }
-        if (r >= real_keys) {
-          const uint32_t vrow = sbase + kVOff + st * kTileBytes + r * 128;
+        if (r < kKeys && r >= real_keys) {
+          const uint32_t vrow = sbase + kVOff + st * kKVBytes + r * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             st_shared_zero16(vrow + c * 16);
-            st_shared_zero16(vrow + kHalfBytes + c * 16);
+            st_shared_zero16(vrow + kKVHalf + c * 16);
           }
         }
       }
-      // P row -> BF16, 128-byte swizzled K-major layout
+      // P row -> BF16, 128-byte swizzled K-major layout (64 keys = 8 chunks)
       const uint32_t prow = sbase + kPOff + r * 128;
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < 8; ++c) {
         const uint32_t w0 = pack_bf16x2(s[8 * c + 0], s[8 * c + 1]);
         const uint32_t w1 = pack_bf16x2(s[8 * c + 2], s[8 * c + 3]);
         const uint32_t w2 = pack_bf16x2(s[8 * c + 4], s[8 * c + 5]);
         const uint32_t w3 = pack_bf16x2(s[8 * c + 6], s[8 * c + 7]);
-        const uint32_t chunk = uint32_t((c & 7) ^ (r & 7));
-        st_shared_v4(prow + (c >> 3) * kHalfBytes + chunk * 16, w0, w1, w2, w3);
+        st_shared_v4(prow + uint32_t((c ^ (r & 7)) * 16), w0, w1, w2, w3);
       }
       fence_proxy_async_smem();
+      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t o0[32], o1[32];
+          const uint32_t oaddr = trow + kOCol + half * 64;
+          tmem_ld32(oaddr, o0);
+          tmem_ld32(oaddr + 32, o1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            o0[i] = __float_as_uint(__uint_as_float(o0[i]) * alpha);
+            o1[i] = __float_as_uint(__uint_as_float(o1[i]) * alpha);
+          }
+          tmem_st32(oaddr, o0);
+          tmem_st32(oaddr + 32, o1);
+        }
+        tmem_st_wait();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kPFull]);
@@ -407,24 +449,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long tok = (long long)q_begin + q0 + rq;
       __nv_bfloat16* dst = p.out + (tok * p.qh + head) * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t raw[32];
-        tmem_ld32(trow + kOCol + c * 32, raw);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t o0[32], o1[32];
+        tmem_ld32(trow + kOCol + half * 64, o0);
+        tmem_ld32(trow + kOCol + half * 64 + 32, o1);
         tmem_ld_wait();
         if (valid_row) {
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
+          for (int v = 0; v < 8; ++v) {
+            const uint32_t* src = v < 4 ? o0 + 8 * v : o1 + 8 * (v - 4);
             uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(raw[8 * v + 0]) * inv, __uint_as_float(raw[8 * v + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(raw[8 * v + 2]) * inv, __uint_as_float(raw[8 * v + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(raw[8 * v + 4]) * inv, __uint_as_float(raw[8 * v + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(raw[8 * v + 6]) * inv, __uint_as_float(raw[8 * v + 7]) * inv);
-            *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = w;
+            w.x = pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
+            *reinterpret_cast<uint4*>(dst + half * 64 + v * 8) = w;
           }
         }
       }
-      if (valid_row && p.lse)
-        p.lse[((long long)b * p.qh + head) * p.max_q + q0 + rq] = l > 0.0f ? (m + fast_log2(l)) * kLn2 : -INFINITY;
+      if (valid_row && p.lse) {
+        const float m_out = m_used == -INFINITY ? 0.0f : m_used;
+        p.lse[((long long)b * p.qh + head) * p.max_q + q0 + rq] =
+            l > 0.0f ? (m_out + fast_log2(l)) * kLn2 : -INFINITY;
+      }
     }
   }
 
@@ -471,7 +518,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   {
     const uint64_t dims[3] = {128, uint64_t(a.kvh), uint64_t(a.num_blocks) * uint64_t(a.block_size)};
     const uint64_t strides[2] = {256, uint64_t(a.kvh) * 256};
-    const uint32_t box[3] = {64, 1, 128};
+    const uint32_t box[3] = {64, 1, uint32_t(kKeys)};
     if (make_map_3d(a.k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, &kmap)) return cudaErrorInvalidValue;
     if (make_map_3d(a.v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, &vmap)) return cudaErrorInvalidValue;
   }
@@ -482,6 +529,9 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit)) {
     e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
