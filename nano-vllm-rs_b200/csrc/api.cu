@@ -115,11 +115,11 @@ int make_map_3d(const void* base, const uint64_t dims[3], const uint64_t strides
 
 namespace api_detail {
 
-// Decode tiles: [tokens][kv_heads][128] with a {128, 1, 32} box.
+// Decode tiles: [tokens][kv_heads][128] with a {128, 1, kDecodeTile} box.
 int kv_decode_map(const void* cache, long long tokens, int kvh, const CUtensorMap** out) {
   const uint64_t dims[3] = {128, uint64_t(kvh), uint64_t(tokens)};
   const uint64_t strides[2] = {256, uint64_t(kvh) * 256};
-  const uint32_t box[3] = {128, 1, 32};
+  const uint32_t box[3] = {128, 1, uint32_t(kDecodeTile)};
   return make_map_3d(cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE, out);
 }
 

@@ -14,14 +14,22 @@
 //  * Warp 0 is a TMA producer: a 3-D tensor map over the cache
 //    [tokens = num_blocks * block_size, kv_heads, 128] loads 32-token K and V
 //    tiles (8 KB each, box {128, 1, 32}) of the sequence's pages into a
-//    6-stage shared-memory ring tracked by mbarriers. A 32-token tile never
-//    crosses a page because block_size is a multiple of 32.
+//    6-stage shared-memory ring. A 32-token tile never crosses a page
+//    because block_size is a multiple of 32.
 //  * Warps 1..4 are consumers; consumer w owns tiles w, w+4, ... and keeps
 //    its own online-softmax state (m, l, O). Each lane owns 8 of the 128
 //    head dimensions (one 16-byte shared-memory load per K/V row); the two
 //    half-warps take alternate tokens. QK partial sums are reduced with a
 //    transpose-reduce shuffle (each step halves the values a lane holds), so
 //    a 16-token dot product costs ~1 shuffle per token instead of 4.
+//  * Phase tracking: mbarrier parity waits are only sound when a waiter is
+//    never two phases behind or ahead of its barrier. With 6 stages shared
+//    round-robin by 4 warps a warp meets a given stage only every other use,
+//    so each stage has two "full" barriers, one for its even and one for its
+//    odd uses. Use k-2 of a stage is tile i-12, which belongs to the same
+//    warp (12 = 0 mod 4), so each warp waits on every phase of the barriers
+//    it uses, in order. The producer waits on every phase of the "empty"
+//    barriers.
 //  * At the end the four warp states merge through shared memory, and the
 //    CTA writes the final BF16 output (1 split) or a normalised FP32 partial
 //    plus its natural-log LSE (several splits) for the combine kernel.
@@ -31,7 +39,7 @@ namespace nvb {
 
 namespace decode_detail {
 
-constexpr int kTile = 32;
+constexpr int kTile = kDecodeTile;  // tokens per pipeline stage
 constexpr int kStages = 6;
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = 32 * (1 + kConsumerWarps);
@@ -47,12 +55,14 @@ struct Smem {
   static constexpr int kPOff = kStages * kStageBytes;                        // P scratch per warp
   static constexpr int kPBytes = kConsumerWarps * GC * kTile * 4;
   static constexpr int kBarOff = kPOff + kPBytes;                            // full[], empty[]
-  static constexpr int kPageOff = kBarOff + 2 * kStages * 8;
+  static constexpr int kPageOff = kBarOff + 3 * kStages * 8;  // full[2 * kStages], empty[kStages]
   static constexpr int kValidOff = kPageOff + kMaxPageCache * 4;
   static constexpr int kBytes = kValidOff + kStages * 4;
   // Merge area reuses the stage ring after the pipeline has drained.
   static constexpr int kMergeBytes = kConsumerWarps * GC * (2 + 128) * 4;
   static_assert(kMergeBytes <= kStages * kStageBytes, "merge area must fit in the stage ring");
+  static_assert((2 * kStages) % kConsumerWarps == 0,
+                "uses k and k-2 of a stage must belong to the same consumer warp");
 };
 
 template <int GC>
@@ -79,9 +89,10 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const DecodeParams p,
                                                           const __grid_constant__ CUtensorMap kmap,
                                                           const __grid_constant__ CUtensorMap vmap) {
   using S = Smem<GC>;
-  constexpr int kTok = GC <= 4 ? 16 : 8;  // tokens per half-warp per pass
-  constexpr int kPasses = kTile / (2 * kTok);
-  constexpr int kShift = kTok == 16 ? 0 : 1;  // after the reduce, lane s holds token s >> kShift
+  constexpr int kHalfTok = kTile / 2;          // tokens per half-warp per tile
+  constexpr int kTok = GC <= 4 ? 16 : 8;       // tokens per half-warp per pass
+  constexpr int kPasses = kHalfTok / kTok;
+  constexpr int kShift = kTok == 16 ? 0 : 1;   // after the reduce, lane s holds token s >> kShift
   extern __shared__ __align__(1024) unsigned char smem[];
 
   int cta = blockIdx.x;
@@ -135,7 +146,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const DecodeParams p,
   }
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
-  uint64_t* empty = full + kStages;
+  uint64_t* empty = full + 2 * kStages;  // full[2 * stage + (use & 1)]
   int* pages = reinterpret_cast<int*>(smem + S::kPageOff);
   int* stage_valid = reinterpret_cast<int*>(smem + S::kValidOff);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -146,7 +157,8 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const DecodeParams p,
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[2 * s], 1);
+      mbar_init(&full[2 * s + 1], 1);
       mbar_init(&empty[s], 1);
     }
     fence_barrier_init();
@@ -172,15 +184,16 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const DecodeParams p,
         const int offset = token0 - logical * p.block_size;
         const int page = cache_pages ? pages[logical - first_page] : table[logical];
         const bool ok = page >= 0 && page < p.num_blocks;
+        uint64_t* fb = &full[2 * stage + ((i / kStages) & 1)];
         stage_valid[stage] = ok ? 1 : 0;
         if (ok) {
           unsigned char* kdst = smem + S::kStageOff + stage * kStageBytes;
           const int trow = page * p.block_size + offset;
-          mbar_arrive_expect_tx(&full[stage], kStageBytes);
-          tma_load_3d_hint(kdst, &kmap, &full[stage], 0, kvhead, trow, policy);
-          tma_load_3d_hint(kdst + kTileBytes, &vmap, &full[stage], 0, kvhead, trow, policy);
+          mbar_arrive_expect_tx(fb, kStageBytes);
+          tma_load_3d_hint(kdst, &kmap, fb, 0, kvhead, trow, policy);
+          tma_load_3d_hint(kdst + kTileBytes, &vmap, fb, 0, kvhead, trow, policy);
         } else {
-          mbar_arrive(&full[stage]);
+          mbar_arrive(fb);
         }
       }
     }
@@ -206,12 +219,13 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const DecodeParams p,
 #pragma unroll
     for (int d = 0; d < 8; ++d) o[g][d] = 0.0f;
   }
-  float* P = reinterpret_cast<float*>(smem + S::kPOff) + cw * GC * kTile;  // [g][h][16]
+  float* P = reinterpret_cast<float*>(smem + S::kPOff) + cw * GC * kTile;  // [g][h][kHalfTok]
   const bool dup_writer = (s & ((1 << kShift) - 1)) == 0;
 
   for (int i = cw; i < ntiles; i += kConsumerWarps) {
     const int stage = i % kStages;
-    if (!mbar_wait(&full[stage], (i / kStages) & 1, kErrDecodeFullWait)) break;
+    const int use = i / kStages;
+    if (!mbar_wait(&full[2 * stage + (use & 1)], (use >> 1) & 1, kErrDecodeFullWait)) break;
     const bool ok = stage_valid[stage] != 0;
     const int ntok = min(kTile, len - (t0 + i) * kTile);
     const unsigned char* kt = smem + S::kStageOff + stage * kStageBytes;
@@ -284,7 +298,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const DecodeParams p,
         const float pr = (sc[pp][g] == -INFINITY) ? 0.0f : fast_exp2(sc[pp][g] - m_new);
         if (dup_writer) {
           l[g] += pr;
-          P[g * kTile + h * 16 + pp * kTok + (s >> kShift)] = pr;
+          P[g * kTile + h * kHalfTok + pp * kTok + (s >> kShift)] = pr;
         }
       }
     }
@@ -292,10 +306,10 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const DecodeParams p,
 
     // ---- O += P V over this half-warp's 16 tokens
     if (ok) {
-      const float* Ph = P + h * 16;
+      const float* Ph = P + h * kHalfTok;
       if (ntok == kTile) {
 #pragma unroll
-        for (int j4 = 0; j4 < 16; j4 += 4) {
+        for (int j4 = 0; j4 < kHalfTok; j4 += 4) {
           float4 pr[GC];
 #pragma unroll
           for (int g = 0; g < GC; ++g) pr[g] = *reinterpret_cast<const float4*>(Ph + g * kTile + j4);

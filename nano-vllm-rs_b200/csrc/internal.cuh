@@ -17,6 +17,9 @@ enum DecodeMode : int {
   kModeVarlen = 2,  // one CTA per query row of a varlen batch: seq_map = cu_q, lens = kv_lens
 };
 
+// Tokens per decode pipeline stage (TMA box {128, 1, kDecodeTile}).
+constexpr int kDecodeTile = 32;
+
 struct DecodeParams {
   const __nv_bfloat16* q;   // [rows, qh, 128]
   __nv_bfloat16* out;       // [rows, qh, 128]

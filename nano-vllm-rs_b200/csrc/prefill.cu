@@ -15,9 +15,9 @@
 //   S_j = Q K_j^T   tcgen05.mma kind::f16, M=128 N=64 K=128 (8 x K16), A and
 //                   B from 128B-swizzled shared memory, D in TMEM (FP32)
 //   P_j = exp2(S_j * scale*log2e - m)   4 softmax warps, one TMEM lane (row)
-//                   per thread, written to swizzled shared memory as BF16
-//   O  += P_j V_j   tcgen05.mma M=128 N=128 K=64, V as an MN-major B operand,
-//                   O in TMEM
+//                   per thread, written back over S_j in TMEM as packed BF16
+//   O  += P_j V_j   tcgen05.mma M=128 N=128 K=64 with A (P) read from TMEM,
+//                   V as an MN-major B operand from shared memory, O in TMEM
 //
 // Warp roles: warp 0 issues TMA (Q once, then a 2-stage K ring and a 2-stage V
 // ring over the sequence's pages: 3-D tensor maps over [tokens, kv_heads,
@@ -25,13 +25,15 @@
 // a page since block_size is a multiple of 256); warp 1 owns TMEM (256
 // columns: S double buffer at 0 and 64, O at 128) and one thread issues the
 // MMAs and tcgen05.commit arrivals; warps 2..5 run the online softmax, the O
-// rescale (TMEM ld/st) and the epilogue. S is double-buffered so the MMA of
-// S_{j+1} overlaps the softmax of S_j, and PV_{j-1} overlaps it as well.
+// rescale (TMEM ld/st) and the epilogue. S/P is double-buffered in TMEM and
+// a buffer is released by the commit of the PV MMA that read its P; the
+// softmax of tile j computes and stores P_j before it waits for PV_{j-1}.
 //
-// Sizing for B200: 112 KB of tiles + 1 KB of barriers per CTA and 256 TMEM
-// columns let two CTAs share an SM (2 x 114 KB of the 228 KB, 2 x 256 of the
-// 512 columns), so one CTA's softmax runs while the other's MMAs use the
-// tensor core, and their prologues/epilogues overlap. The softmax keeps the
+// Sizing for B200: 96 KB of tiles + 1 KB of barriers per CTA and 256 TMEM
+// columns let two CTAs share an SM (2 x 256 of the 512 columns), so one CTA's
+// softmax runs while the other's MMAs use the tensor core, and their
+// prologues/epilogues overlap. A quarter of the exponentials are evaluated
+// on the FMA pipe (exp2_fma) to offload the 16-per-clock MUFU unit. The softmax keeps the
 // running max it scales by unless a row's max grows by more than 2^8
 // (FA4-style lazy rescale: P stays <= 256, exact after the final divide), so
 // the TMEM read-modify-write of O is rare after the first tiles.
@@ -51,7 +53,6 @@ constexpr int kQHalf = kRows * 128;          // 128 rows x 64 BF16 (one 128-byte
 constexpr int kQBytes = 2 * kQHalf;          // Q tile 128 x 128 BF16
 constexpr int kKVHalf = kKeys * 128;         // 64 keys x 64 BF16
 constexpr int kKVBytes = 2 * kKVHalf;        // K or V tile 64 x 128 BF16
-constexpr int kPBytes = kRows * 128;         // P tile 128 x 64 BF16
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 256;
 constexpr int kOCol = 128;
@@ -67,9 +68,8 @@ constexpr int kHeadBytes = kTmemSlotOff + 16;
 constexpr int kQOff = 0;                      // offsets from the aligned tile base
 constexpr int kKOff = kQOff + kQBytes;
 constexpr int kVOff = kKOff + kStages * kKVBytes;
-constexpr int kPOff = kVOff + kStages * kKVBytes;
-constexpr int kTileBytes = kPOff + kPBytes;   // 112 KB
-constexpr int kSmemBytes = 1024 + kTileBytes; // 113 KB: two CTAs per SM
+constexpr int kTileBytes = kVOff + kStages * kKVBytes;  // 96 KB
+constexpr int kSmemBytes = 1024 + kTileBytes;           // 97 KB: two CTAs per SM
 
 struct PrefillParams {
   const int* cu_q;
@@ -111,6 +111,36 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                : "memory");
+}
+
+// O += P V with A (P, packed BF16 pairs) read from tensor memory.
+__device__ __forceinline__ void umma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                                 uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// 2^x on the FMA/ALU pipes for x <= 128 (used for part of the softmax so the
+// MUFU unit is not the limit). Range reduction x = n + f with n the nearest
+// integer (1.5 * 2^23 rounding trick, |f| <= 1/2), then a degree-4
+// polynomial for 2^f fitted to minimise relative error on [-1/2, 1/2] (this
+// file's own fit; max relative error 2.7e-6 in FP32), then n is added to the
+// exponent field. Inputs below -125 (masked keys are -inf) return exactly 0;
+// the clamp keeps the exponent add from leaving the normal range.
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float xc = fmaxf(x, -125.0f);
+  const float t = xc + 12582912.0f;  // 1.5 * 2^23: low mantissa bits hold round(xc)
+  const float f = xc - (t - 12582912.0f);
+  float p = 0.009570096619427204f;
+  p = fmaf(p, f, 0.05591785907745361f);
+  p = fmaf(p, f, 0.240247443318367f);
+  p = fmaf(p, f, 0.6931217908859253f);
+  p = fmaf(p, f, 0.9999992847442627f);
+  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+  return x < -125.0f ? 0.0f : r;
 }
 
 #define NVB_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), \
@@ -208,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[kSFull + s], 1);
-      mbar_init(&bars[kSFree + s], 4);
+      mbar_init(&bars[kSFree + s], 1);
     }
     mbar_init(&bars[kPFull], 4);
     mbar_init(&bars[kODone], 1);
@@ -277,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       bool alive = mbar_wait(&bars[kQFull], 0, kErrPrefillWait);
       tc_fence_after();
-      const uint32_t q_addr = sbase + kQOff, p_addr = sbase + kPOff;
+      const uint32_t q_addr = sbase + kQOff;
       auto issue_pv = [&](int t) {
         const int st = t % kStages;
         alive = alive && mbar_wait(&bars[kPFull], t & 1, kErrPrefillWait);
@@ -285,14 +315,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!alive) return;
         tc_fence_after();
         const uint32_t v_addr = sbase + kVOff + st * kKVBytes;
+        const uint32_t p_tmem = tmem + (t & 1) * kKeys;  // P_t over S_t: 16 keys = 8 columns
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk) {
-          const uint64_t a = sw128_desc(p_addr + kk * 32, 16, 1024);
           const uint64_t bd = sw128_desc(v_addr + kk * 2048, kKVHalf, 1024);
-          umma_bf16(tmem + kOCol, a, bd, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_tmem_a(tmem + kOCol, p_tmem + kk * 8, bd, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars[kVEmpty + st]);
         umma_commit(&bars[kODone]);
+        umma_commit(&bars[kSFree + (t & 1)]);  // S/P buffer free once PV_t has read P_t
       };
       for (int j = 0; j < n_tiles && alive; ++j) {
         const int st = j % kStages, sb = j & 1;
@@ -346,10 +377,6 @@ __global__ void __launch_bounds__(kThreads, 2)
           s[32 + i] = __uint_as_float(raw1[i]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[kSFree + sb]);
-
       if (j >= full_tiles || !ok) {
         const int lim = ok ? min(limit, kv_len - 1) - key0 : -1;
 #pragma unroll
@@ -377,11 +404,22 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int i = 0; i < 8; ++i) sum8[i] = 0.0f;
 #pragma unroll
       for (int c = 0; c < kKeys; ++c) {
-        s[c] = fast_exp2(fmaf(s[c], sl2, -m_exp));
+        const float x = fmaf(s[c], sl2, -m_exp);
+        s[c] = (c & 3) == 3 ? exp2_fma(x) : fast_exp2(x);
         sum8[c & 7] += s[c];
       }
       l = l * alpha + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
 
+      // P_j as packed BF16 pairs over the first 32 columns of S_j.
+      {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(s[2 * i], s[2 * i + 1]);
+        tmem_st32(trow + sb * kKeys, pk);
+      }
+      // Every tile consumes one o_done phase (PV_{j-1} complete): mbarrier
+      // parity waits are only sound when the waiter never falls two phases
+      // behind. By now PV_{j-1} has usually finished.
       if (j >= 1) {
         if (!mbar_wait(&bars[kODone], (j - 1) & 1, kErrPrefillWait)) {
           alive = false;
@@ -390,7 +428,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc_fence_after();
       }
       // V rows that are not real keys (past kv_len, or an invalid page) are
-      // zeroed so that P = 0 never meets a non-finite cache value.
+      // zeroed so that P = 0 never meets a non-finite cache value. PV_{j-1}
+      // done implies V_{j-2} landed, so this vfull wait is for V_j itself.
       const int real_keys = ok ? min(kKeys, kv_len - key0) : 0;
       if (real_keys < kKeys) {
         const int st = j % kStages;
@@ -406,18 +445,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             st_shared_zero16(vrow + kKVHalf + c * 16);
           }
         }
+        fence_proxy_async_smem();
       }
-      // P row -> BF16, 128-byte swizzled K-major layout (64 keys = 8 chunks)
-      const uint32_t prow = sbase + kPOff + r * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t w0 = pack_bf16x2(s[8 * c + 0], s[8 * c + 1]);
-        const uint32_t w1 = pack_bf16x2(s[8 * c + 2], s[8 * c + 3]);
-        const uint32_t w2 = pack_bf16x2(s[8 * c + 4], s[8 * c + 5]);
-        const uint32_t w3 = pack_bf16x2(s[8 * c + 6], s[8 * c + 7]);
-        st_shared_v4(prow + uint32_t((c ^ (r & 7)) * 16), w0, w1, w2, w3);
-      }
-      fence_proxy_async_smem();
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
@@ -434,8 +463,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           tmem_st32(oaddr, o0);
           tmem_st32(oaddr + 32, o1);
         }
-        tmem_st_wait();
       }
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kPFull]);
