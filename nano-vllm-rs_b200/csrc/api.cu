@@ -125,10 +125,30 @@ int kv_decode_map(const void* cache, long long tokens, int kvh, const CUtensorMa
 
 constexpr float kScaleLog2 = 1.4426950408889634f / 11.313708498984761f;  // log2(e) / sqrt(128)
 
+// tcgen05 decode tiles: [tokens][kv_heads][128] with a {64, 1, 128} box, 128B swizzle.
+int kv_mma_map(const void* cache, long long tokens, int kvh, const CUtensorMap** out) {
+  const uint64_t dims[3] = {128, uint64_t(kvh), uint64_t(tokens)};
+  const uint64_t strides[2] = {256, uint64_t(kvh) * 256};
+  const uint32_t box[3] = {64, 1, 128};
+  return make_map_3d(cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, out);
+}
+
 int run_decode(cudaStream_t stream, DecodeParams p, const void* k, const void* v) {
   const long long tokens = (long long)p.num_blocks * p.block_size;
   const CUtensorMap* kmap = nullptr;
   const CUtensorMap* vmap = nullptr;
+  p.scale_log2 = kScaleLog2;
+  if (p.mode == kModeDecode && p.block_size % 128 == 0 && p.qh / p.kvh <= 16) {
+    if (int rc = kv_mma_map(k, tokens, p.kvh, &kmap)) return rc;
+    if (int rc = kv_mma_map(v, tokens, p.kvh, &vmap)) return rc;
+    p.n_hgroups = 1;
+    cudaError_t e = launch_decode_mma(p, *kmap, *vmap, stream);
+    if (e != cudaErrorNotSupported) {
+      if (e == cudaSuccess && p.num_splits > 1) e = launch_combine(p, stream);
+      return cuda_status(e, "decode attention launch");
+    }
+    cudaGetLastError();
+  }
   if (int rc = kv_decode_map(k, tokens, p.kvh, &kmap)) return rc;
   if (int rc = kv_decode_map(v, tokens, p.kvh, &vmap)) return rc;
   p.scale_log2 = kScaleLog2;

@@ -492,6 +492,11 @@ cudaError_t launch_decode(DecodeParams p, const CUtensorMap& kmap, const CUtenso
     default: e = launch_gc<8>(p, kmap, vmap, stream); break;
   }
   if (e != cudaSuccess || p.num_splits == 1) return e;
+  return launch_combine(p, stream);
+}
+
+cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream) {
+  using namespace decode_detail;
   const long long items = (long long)p.rows * p.qh;
   const long long grid = (items + 7) / 8;
   combine_kernel<<<unsigned(grid), 256, 0, stream>>>(p.lse_accum, p.out_accum, p.out, p.lse, p.rows, p.qh,

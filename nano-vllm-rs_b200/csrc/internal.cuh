@@ -37,7 +37,13 @@ struct DecodeParams {
 
 cudaError_t launch_decode(DecodeParams p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                           cudaStream_t stream);
+// tcgen05 decode (decode_mma.cu); cudaErrorNotSupported when it does not
+// cover the shape. Takes tensor maps with a {64, 1, 128} 128B-swizzled box.
+cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                              cudaStream_t stream);
 int decode_group_chunk(int group);
+// Split-KV combine of lse_accum / out_accum into out (and lse).
+cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream);
 
 cudaError_t launch_qkv_rope(cudaStream_t stream, bool cached, const void* qkv, const void* qw,
                             const void* kw, const int* positions, const int* slots, void* qout,
