@@ -458,7 +458,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": profile_traffic(),
                          "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
-                         "kernel": "decode_kernel", "algorithmic_bytes_per_launch": step_bytes,
+                         "kernel": "decode_mma_kernel", "algorithmic_bytes_per_launch": step_bytes,
                          "launch_ms": round(launch_ms, 5), "launch_ms_first10": round(launch_first, 5),
                          "launch_ms_last10": round(launch_last, 5)},
             "tok_s": round(world * batch / (ms_per_step / 1e3), 1),
@@ -470,7 +470,7 @@ def main():
                 "ms_per_step": round(e2e_ms / e2e_steps, 5),
                 "path": "pinned H2D of step inputs -> nvb_qkv_rope_cached -> nvb_paged_fwd_ex -> D2H output"},
             "gpu_launches": args.steps * (1 if splits == 1 else 2),
-            "gpu_launches_note": "decode_kernel launches (+ combine_kernel when num_splits > 1) in the timed region",
+            "gpu_launches_note": "decode_mma_kernel launches (+ combine_kernel when num_splits > 1) in the timed region",
             "clocks": clock_rec,
             "cpu_baseline": cpu,
         }
