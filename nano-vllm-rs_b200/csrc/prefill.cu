@@ -32,8 +32,10 @@
 // Sizing for B200: 96 KB of tiles + 1 KB of barriers per CTA and 256 TMEM
 // columns let two CTAs share an SM (2 x 256 of the 512 columns), so one CTA's
 // softmax runs while the other's MMAs use the tensor core, and their
-// prologues/epilogues overlap. A quarter of the exponentials are evaluated
-// on the FMA pipe (exp2_fma) to offload the 16-per-clock MUFU unit. The softmax keeps the
+// prologues/epilogues overlap. The softmax uses Blackwell's packed FP32x2
+// FMA/ADD and three-input max to cut its instruction count, and evaluates an
+// eighth of the exponentials on the FMA pipe (exp2_fma) next to the
+// 16-per-clock MUFU unit. Page ids are cached in shared memory at CTA start. The softmax keeps the
 // running max it scales by unless a row's max grows by more than 2^8
 // (FA4-style lazy rescale: P stays <= 256, exact after the final divide), so
 // the TMEM read-modify-write of O is rare after the first tiles.
@@ -68,8 +70,10 @@ constexpr int kHeadBytes = kTmemSlotOff + 16;
 constexpr int kQOff = 0;                      // offsets from the aligned tile base
 constexpr int kKOff = kQOff + kQBytes;
 constexpr int kVOff = kKOff + kStages * kKVBytes;
-constexpr int kTileBytes = kVOff + kStages * kKVBytes;  // 96 KB
-constexpr int kSmemBytes = 1024 + kTileBytes;           // 97 KB: two CTAs per SM
+constexpr int kPageOff = kVOff + kStages * kKVBytes;    // int page ids of the sequence
+constexpr int kMaxPages = 1024;                          // cached; longer contexts read the table
+constexpr int kTileBytes = kPageOff + kMaxPages * 4;    // 100 KB
+constexpr int kSmemBytes = 1024 + kTileBytes;           // 101 KB: two CTAs per SM
 
 struct PrefillParams {
   const int* cu_q;
@@ -141,6 +145,47 @@ __device__ __forceinline__ float exp2_fma(float x) {
   p = fmaf(p, f, 0.9999992847442627f);
   const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
   return x < -125.0f ? 0.0f : r;
+}
+
+// Packed FP32 pairs (Blackwell f32x2 ALU forms): d = a * b + c, d = a + b.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                     float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// exp2_fma on a pair of inputs with the packed FP32 forms.
+__device__ __forceinline__ void exp2_fma_pair(float& a, float& b) {
+  const float xa = fmaxf(a, -125.0f), xb = fmaxf(b, -125.0f);
+  float ta, tb, na, nb, fa, fb, pa, pb;
+  add2(ta, tb, xa, xb, 12582912.0f, 12582912.0f);
+  add2(na, nb, ta, tb, -12582912.0f, -12582912.0f);
+  fma2(fa, fb, na, nb, -1.0f, -1.0f, xa, xb);  // f = x - round(x)
+  fma2(pa, pb, 0.009570096619427204f, 0.009570096619427204f, fa, fb, 0.05591785907745361f, 0.05591785907745361f);
+  fma2(pa, pb, pa, pb, fa, fb, 0.240247443318367f, 0.240247443318367f);
+  fma2(pa, pb, pa, pb, fa, fb, 0.6931217908859253f, 0.6931217908859253f);
+  fma2(pa, pb, pa, pb, fa, fb, 0.9999992847442627f, 0.9999992847442627f);
+  const float ra = __int_as_float(__float_as_int(pa) + (__float_as_int(ta) << 23));
+  const float rb = __int_as_float(__float_as_int(pb) + (__float_as_int(tb) << 23));
+  a = a < -125.0f ? 0.0f : ra;
+  b = b < -125.0f ? 0.0f : rb;
 }
 
 #define NVB_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), \
@@ -250,6 +295,12 @@ __global__ void __launch_bounds__(kThreads, 2)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  const int n_pages = (key_end - 1) / p.block_size + 1;
+  const bool cache_pages = n_pages <= kMaxPages;
+  int* pages = reinterpret_cast<int*>(tiles + kPageOff);
+  if (warp == 0 && cache_pages) {
+    for (int i = lane; i < n_pages; i += 32) pages[i] = table[i];
+  }
   if (warp >= 2 && p.rows_used < kRows) {
     // Rows past the packed (query, head) rows are not loaded: zero them.
     const int t = threadIdx.x - 64;
@@ -279,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t par = ((j / kStages) + 1) & 1;
         const int key0 = j * kKeys;
         const int logical = key0 / p.block_size;
-        const int page = table[logical];
+        const int page = cache_pages ? pages[logical] : table[logical];
         const bool ok = page_ok(page, p.num_blocks);
         const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
         if (j >= kStages && !mbar_wait(&bars[kKEmpty + st], par, kErrPrefillWait)) break;
@@ -359,7 +410,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int j = 0; j < n_tiles; ++j) {
       const int sb = j & 1;
       const int key0 = j * kKeys;
-      const bool ok = page_ok(table[key0 / p.block_size], p.num_blocks);
+      const int logical = key0 / p.block_size;
+      const bool ok = page_ok(cache_pages ? pages[logical] : table[logical], p.num_blocks);
       if (!mbar_wait(&bars[kSFull + sb], (j >> 1) & 1, kErrPrefillWait)) {
         alive = false;
         break;
@@ -387,9 +439,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx8[i] = s[i];
 #pragma unroll
-      for (int c = 8; c < kKeys; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      for (int c = 8; c < kKeys; c += 16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = max3(mx8[i], s[c + i], s[c + 8 + i]);
+      }
+      const float mx = max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
       const float m_tile = mx * sl2;
       // Rescale only when the row max grew by more than 2^8 (or on the
       // first finite max); otherwise keep scaling by the stale max.
@@ -398,17 +452,23 @@ __global__ void __launch_bounds__(kThreads, 2)
         alpha = fast_exp2(m_used - m_tile);  // 0 when m_used = -inf
         m_used = m_tile;
       }
-      const float m_exp = m_used == -INFINITY ? 0.0f : m_used;
-      float sum8[8];
+      const float nm = m_used == -INFINITY ? 0.0f : -m_used;
+      float sum[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sum8[i] = 0.0f;
+      for (int i = 0; i < 8; ++i) sum[i] = 0.0f;
 #pragma unroll
-      for (int c = 0; c < kKeys; ++c) {
-        const float x = fmaf(s[c], sl2, -m_exp);
-        s[c] = (c & 3) == 3 ? exp2_fma(x) : fast_exp2(x);
-        sum8[c & 7] += s[c];
+      for (int c = 0; c < kKeys; c += 2) {
+        fma2(s[c], s[c + 1], s[c], s[c + 1], sl2, sl2, nm, nm);
+        if ((c & 15) == 14) {
+          exp2_fma_pair(s[c], s[c + 1]);  // one pair in eight on the FMA pipe
+        } else {
+          s[c] = fast_exp2(s[c]);
+          s[c + 1] = fast_exp2(s[c + 1]);
+        }
+        const int k = (c >> 1) & 3;  // four independent accumulator pairs
+        add2(sum[2 * k], sum[2 * k + 1], sum[2 * k], sum[2 * k + 1], s[c], s[c + 1]);
       }
-      l = l * alpha + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
+      l = l * alpha + (((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7])));
 
       // P_j as packed BF16 pairs over the first 32 columns of S_j.
       {
