@@ -35,7 +35,14 @@
 // prologues/epilogues overlap. The softmax uses Blackwell's packed FP32x2
 // FMA/ADD and three-input max to cut its instruction count, and evaluates an
 // eighth of the exponentials on the FMA pipe (exp2_fma) next to the
-// 16-per-clock MUFU unit. Page ids are cached in shared memory at CTA start. The softmax keeps the
+// 16-per-clock MUFU unit.
+//
+// The kernel is persistent: 2 CTAs per SM loop over (query tile, sequence,
+// kv head) items, longest causal tiles first, keeping their barriers and
+// TMEM; the next item's Q load and first K/V tiles overlap the current
+// item's last tiles and epilogue. Barrier phases are tracked with global
+// tile and item counters; q_free (all S MMAs of an item done) and o_free (its
+// epilogue has read O) guard the two buffers reused across items. The softmax keeps the
 // running max it scales by unless a row's max grows by more than 2^8
 // (FA4-style lazy rescale: P stays <= 256, exact after the final divide), so
 // the TMEM read-modify-write of O is rare after the first tiles.
@@ -64,18 +71,17 @@ constexpr float kRescaleLog2 = 8.0f;         // lazy rescale threshold (P <= 2^8
 // Barriers and the TMEM slot sit below the first 1024-byte boundary; the
 // tiles follow on 1024-byte boundaries (128-byte swizzle atoms).
 enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kSFree = 11, kPFull = 13,
-           kODone = 14, kNumBars = 15 };
+           kODone = 14, kQFree = 15, kOFree = 16, kNumBars = 17 };
 constexpr int kTmemSlotOff = kNumBars * 8;
 constexpr int kHeadBytes = kTmemSlotOff + 16;
 constexpr int kQOff = 0;                      // offsets from the aligned tile base
 constexpr int kKOff = kQOff + kQBytes;
 constexpr int kVOff = kKOff + kStages * kKVBytes;
-constexpr int kPageOff = kVOff + kStages * kKVBytes;    // int page ids of the sequence
-constexpr int kMaxPages = 1024;                          // cached; longer contexts read the table
-constexpr int kTileBytes = kPageOff + kMaxPages * 4;    // 100 KB
-constexpr int kSmemBytes = 1024 + kTileBytes;           // 101 KB: two CTAs per SM
+constexpr int kTileBytes = kVOff + kStages * kKVBytes;  // 96 KB
+constexpr int kSmemBytes = 1024 + kTileBytes;           // 97 KB: two CTAs per SM
 
 struct PrefillParams {
+  int n_qtiles;  // query tiles of the longest sequence
   const int* cu_q;
   const int* kv_lens;
   const int* block_table;
@@ -224,6 +230,39 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 
 __device__ __forceinline__ bool page_ok(int page, int num_blocks) { return page >= 0 && page < num_blocks; }
 
+// One query tile of one (sequence, kv head): the work item of the
+// persistent loop. Virtual items are ordered by query-tile index, longest
+// causal tiles first, and dealt round-robin to the CTAs.
+struct Item {
+  int b, h, q_begin, q_len, q0, qt_eff, kv_len, prefix, key_end, n_tiles, full_tiles;
+  bool empty;
+};
+
+__device__ __forceinline__ Item make_item(const PrefillParams& p, int v) {
+  Item it;
+  const int pairs = p.batch * p.kvh;
+  const int tile = p.n_qtiles - 1 - v / pairs;
+  const int rest = v % pairs;
+  it.b = rest / p.kvh;
+  it.h = rest % p.kvh;
+  it.q_begin = p.cu_q[it.b];
+  it.q_len = p.cu_q[it.b + 1] - it.q_begin;
+  it.q0 = tile * p.qt;
+  it.empty = it.q0 >= it.q_len;
+  it.qt_eff = it.empty ? 0 : min(p.qt, it.q_len - it.q0);
+  it.kv_len = it.empty ? 0 : p.kv_lens[it.b];
+  it.prefix = it.kv_len - it.q_len;
+  // A context longer than the page table, or shorter than its query group,
+  // is invalid input: such rows get zero output (as decode does).
+  const bool seq_ok = !it.empty && it.prefix >= 0 &&
+                      (long long)it.kv_len <= (long long)p.table_stride * p.block_size;
+  it.key_end = seq_ok ? min(it.kv_len, it.prefix + it.q0 + it.qt_eff) : 0;
+  it.n_tiles = it.key_end > 0 ? (it.key_end + kKeys - 1) / kKeys : 0;
+  const int free_keys = min(it.kv_len, it.prefix + it.q0 + 1);  // keys every row of the tile sees
+  it.full_tiles = free_keys > 0 ? free_keys / kKeys : 0;
+  return it;
+}
+
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
                    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
@@ -233,48 +272,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tile_addr = (raw_addr + kHeadBytes + 1023u) & ~1023u;
   unsigned char* tiles = smem_raw + (tile_addr - raw_addr);
   const uint32_t sbase = tile_addr;
-
-  const int tile = gridDim.x - 1 - blockIdx.x;  // longest causal tiles first
-  const int b = blockIdx.y, h = blockIdx.z;
-  const int q_begin = p.cu_q[b];
-  const int q_len = p.cu_q[b + 1] - q_begin;
-  const int q0 = tile * p.qt;
-  if (q0 >= q_len) return;
   if (tile_addr + kTileBytes > raw_addr + kSmemBytes) {  // dynamic smem base not 1 KB friendly
     if (threadIdx.x == 0) record_error(kErrPrefillAlign);
     return;
   }
-  const int kv_len = p.kv_lens[b];
-  const int qt_eff = min(p.qt, q_len - q0);
-  const int prefix = kv_len - q_len;  // keys before this sequence's first query
-  // A context longer than the page table, or shorter than its query group,
-  // is invalid input: such rows get zero output (as decode does).
-  const bool seq_ok = prefix >= 0 && (long long)kv_len <= (long long)p.table_stride * p.block_size;
-  const int key_end = seq_ok ? min(kv_len, prefix + q0 + qt_eff) : 0;
-  const int n_tiles = key_end > 0 ? (key_end + kKeys - 1) / kKeys : 0;
-  const int free_keys = min(kv_len, prefix + q0 + 1);  // keys every row of the tile sees
-  const int full_tiles = free_keys > 0 ? free_keys / kKeys : 0;
+  const int n_items = p.n_qtiles * p.batch * p.kvh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int* table = p.block_table + (long long)b * p.table_stride;
-
-  if (n_tiles == 0) {
-    // No visible keys (invalid context): zero rows, -inf LSE.
-    for (int e = threadIdx.x; e < p.rows_used * 128; e += blockDim.x) {
-      const int r = e >> 7, d = e & 127, rq = r / p.group;
-      if (rq >= qt_eff) continue;
-      const long long tok = (long long)q_begin + q0 + rq;
-      const int head = h * p.group + r % p.group;
-      p.out[(tok * p.qh + head) * 128 + d] = __float2bfloat16_rn(0.0f);
-      if (d == 0 && p.lse) p.lse[((long long)b * p.qh + head) * p.max_q + q0 + rq] = -INFINITY;
-    }
-    return;
-  }
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + kTmemSlotOff);
-
   if (threadIdx.x == 0) {
     mbar_init(&bars[kQFull], 1);
+    mbar_init(&bars[kQFree], 1);
+    mbar_init(&bars[kOFree], 4);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars[kKFull + s], 1);
       mbar_init(&bars[kKEmpty + s], 1);
@@ -295,14 +305,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  const int n_pages = (key_end - 1) / p.block_size + 1;
-  const bool cache_pages = n_pages <= kMaxPages;
-  int* pages = reinterpret_cast<int*>(tiles + kPageOff);
-  if (warp == 0 && cache_pages) {
-    for (int i = lane; i < n_pages; i += 32) pages[i] = table[i];
-  }
   if (warp >= 2 && p.rows_used < kRows) {
-    // Rows past the packed (query, head) rows are not loaded: zero them.
+    // Rows past the packed (query, head) rows are never loaded: zero them once.
     const int t = threadIdx.x - 64;
     for (int e = t; e < (kRows - p.rows_used) * 16; e += 128) {
       const int r = p.rows_used + (e >> 4), c = e & 15;
@@ -321,80 +325,106 @@ __global__ void __launch_bounds__(kThreads, 2)
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      mbar_arrive_expect_tx(&bars[kQFull], 2u * 128u * uint32_t(p.rows_used));
-      const int qy = h * p.group, qz = q_begin + q0;
-      tma_load_3d(tiles + kQOff, &qmap, &bars[kQFull], 0, qy, qz);
-      tma_load_3d(tiles + kQOff + kQHalf, &qmap, &bars[kQFull], 64, qy, qz);
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j % kStages;
-        const uint32_t par = ((j / kStages) + 1) & 1;
-        const int key0 = j * kKeys;
-        const int logical = key0 / p.block_size;
-        const int page = cache_pages ? pages[logical] : table[logical];
-        const bool ok = page_ok(page, p.num_blocks);
-        const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
-        if (j >= kStages && !mbar_wait(&bars[kKEmpty + st], par, kErrPrefillWait)) break;
-        unsigned char* kdst = tiles + kKOff + st * kKVBytes;
-        if (ok) {
-          mbar_arrive_expect_tx(&bars[kKFull + st], kKVBytes);
-          tma_load_3d(kdst, &kmap, &bars[kKFull + st], 0, h, trow);
-          tma_load_3d(kdst + kKVHalf, &kmap, &bars[kKFull + st], 64, h, trow);
-        } else {
-          mbar_arrive(&bars[kKFull + st]);
+      int gt = 0, it_count = 0;
+      bool alive = true;
+      for (int v = blockIdx.x; v < n_items && alive; v += gridDim.x) {
+        const Item it = make_item(p, v);
+        if (it.n_tiles == 0) continue;
+        const int* table = p.block_table + (long long)it.b * p.table_stride;
+        // Q of the previous item is free once all its S MMAs completed.
+        if (it_count > 0 && !mbar_wait(&bars[kQFree], (it_count - 1) & 1, kErrPrefillWait)) break;
+        mbar_arrive_expect_tx(&bars[kQFull], 2u * 128u * uint32_t(p.rows_used));
+        const int qy = it.h * p.group, qz = it.q_begin + it.q0;
+        tma_load_3d(tiles + kQOff, &qmap, &bars[kQFull], 0, qy, qz);
+        tma_load_3d(tiles + kQOff + kQHalf, &qmap, &bars[kQFull], 64, qy, qz);
+        for (int j = 0; j < it.n_tiles; ++j) {
+          const int g = gt + j;
+          const int st = g % kStages;
+          const uint32_t par = ((g / kStages) + 1) & 1;
+          const int key0 = j * kKeys;
+          const int logical = key0 / p.block_size;
+          const int page = table[logical];
+          const bool ok = page_ok(page, p.num_blocks);
+          const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
+          if (g >= kStages && !mbar_wait(&bars[kKEmpty + st], par, kErrPrefillWait)) { alive = false; break; }
+          unsigned char* kdst = tiles + kKOff + st * kKVBytes;
+          if (ok) {
+            mbar_arrive_expect_tx(&bars[kKFull + st], kKVBytes);
+            tma_load_3d(kdst, &kmap, &bars[kKFull + st], 0, it.h, trow);
+            tma_load_3d(kdst + kKVHalf, &kmap, &bars[kKFull + st], 64, it.h, trow);
+          } else {
+            mbar_arrive(&bars[kKFull + st]);
+          }
+          if (g >= kStages && !mbar_wait(&bars[kVEmpty + st], par, kErrPrefillWait)) { alive = false; break; }
+          unsigned char* vdst = tiles + kVOff + st * kKVBytes;
+          if (ok) {
+            mbar_arrive_expect_tx(&bars[kVFull + st], kKVBytes);
+            tma_load_3d(vdst, &vmap, &bars[kVFull + st], 0, it.h, trow);
+            tma_load_3d(vdst + kKVHalf, &vmap, &bars[kVFull + st], 64, it.h, trow);
+          } else {
+            mbar_arrive(&bars[kVFull + st]);
+          }
         }
-        if (j >= kStages && !mbar_wait(&bars[kVEmpty + st], par, kErrPrefillWait)) break;
-        unsigned char* vdst = tiles + kVOff + st * kKVBytes;
-        if (ok) {
-          mbar_arrive_expect_tx(&bars[kVFull + st], kKVBytes);
-          tma_load_3d(vdst, &vmap, &bars[kVFull + st], 0, h, trow);
-          tma_load_3d(vdst + kKVHalf, &vmap, &bars[kVFull + st], 64, h, trow);
-        } else {
-          mbar_arrive(&bars[kVFull + st]);
-        }
+        gt += it.n_tiles;
+        ++it_count;
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      bool alive = mbar_wait(&bars[kQFull], 0, kErrPrefillWait);
-      tc_fence_after();
       const uint32_t q_addr = sbase + kQOff;
-      auto issue_pv = [&](int t) {
-        const int st = t % kStages;
-        alive = alive && mbar_wait(&bars[kPFull], t & 1, kErrPrefillWait);
-        alive = alive && mbar_wait(&bars[kVFull + st], (t / kStages) & 1, kErrPrefillWait);
+      int gt = 0, it_count = 0;
+      bool alive = true;
+      // PV for global tile g; `first` starts a new item's accumulator, which
+      // must wait until the previous item's epilogue has read O.
+      auto issue_pv = [&](int g, bool first) {
+        const int st = g % kStages;
+        if (first && it_count > 0) alive = alive && mbar_wait(&bars[kOFree], (it_count - 1) & 1, kErrPrefillWait);
+        alive = alive && mbar_wait(&bars[kPFull], g & 1, kErrPrefillWait);
+        alive = alive && mbar_wait(&bars[kVFull + st], (g / kStages) & 1, kErrPrefillWait);
         if (!alive) return;
         tc_fence_after();
         const uint32_t v_addr = sbase + kVOff + st * kKVBytes;
-        const uint32_t p_tmem = tmem + (t & 1) * kKeys;  // P_t over S_t: 16 keys = 8 columns
+        const uint32_t p_tmem = tmem + (g & 1) * kKeys;  // P_g over S_g: 16 keys = 8 columns
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk) {
           const uint64_t bd = sw128_desc(v_addr + kk * 2048, kKVHalf, 1024);
-          umma_bf16_tmem_a(tmem + kOCol, p_tmem + kk * 8, bd, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_tmem_a(tmem + kOCol, p_tmem + kk * 8, bd, kIdescPV, (!first || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars[kVEmpty + st]);
         umma_commit(&bars[kODone]);
-        umma_commit(&bars[kSFree + (t & 1)]);  // S/P buffer free once PV_t has read P_t
+        umma_commit(&bars[kSFree + (g & 1)]);  // S/P buffer free once PV_g has read P_g
       };
-      for (int j = 0; j < n_tiles && alive; ++j) {
-        const int st = j % kStages, sb = j & 1;
-        alive = mbar_wait(&bars[kKFull + st], (j / kStages) & 1, kErrPrefillWait);
-        if (alive && j >= 2) alive = mbar_wait(&bars[kSFree + sb], ((j >> 1) + 1) & 1, kErrPrefillWait);
-        if (!alive) break;
+      for (int v = blockIdx.x; v < n_items && alive; v += gridDim.x) {
+        const Item it = make_item(p, v);
+        if (it.n_tiles == 0) continue;
+        alive = mbar_wait(&bars[kQFull], it_count & 1, kErrPrefillWait);
         tc_fence_after();
-        const uint32_t k_addr = sbase + kKOff + st * kKVBytes;
+        for (int j = 0; j < it.n_tiles && alive; ++j) {
+          const int g = gt + j;
+          const int st = g % kStages, sb = g & 1;
+          alive = mbar_wait(&bars[kKFull + st], (g / kStages) & 1, kErrPrefillWait);
+          if (alive && g >= 2) alive = mbar_wait(&bars[kSFree + sb], ((g >> 1) + 1) & 1, kErrPrefillWait);
+          if (!alive) break;
+          tc_fence_after();
+          const uint32_t k_addr = sbase + kKOff + st * kKVBytes;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
-          const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-          umma_bf16(tmem + sb * kKeys, sw128_desc(q_addr + qoff, 16, 1024), sw128_desc(k_addr + koff, 16, 1024),
-                    kIdescS, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
+            const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
+            umma_bf16(tmem + sb * kKeys, sw128_desc(q_addr + qoff, 16, 1024), sw128_desc(k_addr + koff, 16, 1024),
+                      kIdescS, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&bars[kKEmpty + st]);
+          umma_commit(&bars[kSFull + sb]);
+          if (j >= 1) issue_pv(g - 1, j == 1);
         }
-        umma_commit(&bars[kKEmpty + st]);
-        umma_commit(&bars[kSFull + sb]);
-        if (j >= 1) issue_pv(j - 1);
+        if (!alive) break;
+        umma_commit(&bars[kQFree]);  // every S MMA of this item has been issued
+        issue_pv(gt + it.n_tiles - 1, it.n_tiles == 1);
+        gt += it.n_tiles;
+        ++it_count;
       }
-      if (alive) issue_pv(n_tiles - 1);
     }
   } else {
     // ---------------------------------------------- softmax and epilogue
@@ -402,140 +432,155 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int r = quad * 32 + lane;  // TMEM lane = packed row
     const uint32_t trow = tmem + (uint32_t(quad * 32) << 16);
     const int rq = r / p.group;
-    const bool valid_row = r < p.rows_used && rq < qt_eff;
-    const int limit = valid_row ? prefix + q0 + rq : key_end - 1;  // last visible key
     const float sl2 = p.scale_log2;
-    float m_used = -INFINITY, l = 0.0f;  // running max the probabilities are scaled by
+    int gt = 0;
     bool alive = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int sb = j & 1;
-      const int key0 = j * kKeys;
-      const int logical = key0 / p.block_size;
-      const bool ok = page_ok(cache_pages ? pages[logical] : table[logical], p.num_blocks);
-      if (!mbar_wait(&bars[kSFull + sb], (j >> 1) & 1, kErrPrefillWait)) {
-        alive = false;
-        break;
-      }
-      tc_fence_after();
-      float s[kKeys];
-      {
-        uint32_t raw0[32], raw1[32];
-        tmem_ld32(trow + sb * kKeys, raw0);
-        tmem_ld32(trow + sb * kKeys + 32, raw1);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          s[i] = __uint_as_float(raw0[i]);
-          s[32 + i] = __uint_as_float(raw1[i]);
+    for (int v = blockIdx.x; v < n_items && alive; v += gridDim.x) {
+      const Item it = make_item(p, v);
+      if (it.empty) continue;
+      const int head = it.h * p.group + (r % p.group);
+      const bool valid_row = r < p.rows_used && rq < it.qt_eff;
+      const long long tok = (long long)it.q_begin + it.q0 + rq;
+      if (it.n_tiles == 0) {
+        // No visible keys (invalid context): zero rows, -inf LSE.
+        if (valid_row) {
+          __nv_bfloat16* dst = p.out + (tok * p.qh + head) * 128;
+          for (int d = 0; d < 128; d += 8) *reinterpret_cast<uint4*>(dst + d) = make_uint4(0, 0, 0, 0);
+          if (p.lse) p.lse[((long long)it.b * p.qh + head) * p.max_q + it.q0 + rq] = -INFINITY;
         }
+        continue;
       }
-      if (j >= full_tiles || !ok) {
-        const int lim = ok ? min(limit, kv_len - 1) - key0 : -1;
-#pragma unroll
-        for (int c = 0; c < kKeys; ++c)
-          if (c > lim) s[c] = -INFINITY;
-      }
-      float mx8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = s[i];
-#pragma unroll
-      for (int c = 8; c < kKeys; c += 16) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = max3(mx8[i], s[c + i], s[c + 8 + i]);
-      }
-      const float mx = max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
-      const float m_tile = mx * sl2;
-      // Rescale only when the row max grew by more than 2^8 (or on the
-      // first finite max); otherwise keep scaling by the stale max.
-      float alpha = 1.0f;
-      if (m_tile > m_used + kRescaleLog2) {
-        alpha = fast_exp2(m_used - m_tile);  // 0 when m_used = -inf
-        m_used = m_tile;
-      }
-      const float nm = m_used == -INFINITY ? 0.0f : -m_used;
-      float sum[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sum[i] = 0.0f;
-#pragma unroll
-      for (int c = 0; c < kKeys; c += 2) {
-        fma2(s[c], s[c + 1], s[c], s[c + 1], sl2, sl2, nm, nm);
-        if ((c & 15) == 14) {
-          exp2_fma_pair(s[c], s[c + 1]);  // one pair in eight on the FMA pipe
-        } else {
-          s[c] = fast_exp2(s[c]);
-          s[c + 1] = fast_exp2(s[c + 1]);
-        }
-        const int k = (c >> 1) & 3;  // four independent accumulator pairs
-        add2(sum[2 * k], sum[2 * k + 1], sum[2 * k], sum[2 * k + 1], s[c], s[c + 1]);
-      }
-      l = l * alpha + (((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7])));
-
-      // P_j as packed BF16 pairs over the first 32 columns of S_j.
-      {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(s[2 * i], s[2 * i + 1]);
-        tmem_st32(trow + sb * kKeys, pk);
-      }
-      // Every tile consumes one o_done phase (PV_{j-1} complete): mbarrier
-      // parity waits are only sound when the waiter never falls two phases
-      // behind. By now PV_{j-1} has usually finished.
-      if (j >= 1) {
-        if (!mbar_wait(&bars[kODone], (j - 1) & 1, kErrPrefillWait)) {
+      const int* table = p.block_table + (long long)it.b * p.table_stride;
+      const int limit = valid_row ? it.prefix + it.q0 + rq : it.key_end - 1;  // last visible key
+      float m_used = -INFINITY, l = 0.0f;  // running max the probabilities are scaled by
+      for (int j = 0; j < it.n_tiles; ++j) {
+        const int g = gt + j;
+        const int sb = g & 1;
+        const int key0 = j * kKeys;
+        const bool ok = page_ok(table[key0 / p.block_size], p.num_blocks);
+        if (!mbar_wait(&bars[kSFull + sb], (g >> 1) & 1, kErrPrefillWait)) {
           alive = false;
           break;
         }
         tc_fence_after();
-      }
-      // V rows that are not real keys (past kv_len, or an invalid page) are
-      // zeroed so that P = 0 never meets a non-finite cache value. PV_{j-1}
-      // done implies V_{j-2} landed, so this vfull wait is for V_j itself.
-      const int real_keys = ok ? min(kKeys, kv_len - key0) : 0;
-      if (real_keys < kKeys) {
-        const int st = j % kStages;
-        if (!mbar_wait(&bars[kVFull + st], (j / kStages) & 1, kErrPrefillWait)) {
-          alive = false;
-          break;
-        }
-        if (r < kKeys && r >= real_keys) {
-          const uint32_t vrow = sbase + kVOff + st * kKVBytes + r * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            st_shared_zero16(vrow + c * 16);
-            st_shared_zero16(vrow + kKVHalf + c * 16);
-          }
-        }
-        fence_proxy_async_smem();
-      }
-      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t o0[32], o1[32];
-          const uint32_t oaddr = trow + kOCol + half * 64;
-          tmem_ld32(oaddr, o0);
-          tmem_ld32(oaddr + 32, o1);
+        float s[kKeys];
+        {
+          uint32_t raw0[32], raw1[32];
+          tmem_ld32(trow + sb * kKeys, raw0);
+          tmem_ld32(trow + sb * kKeys + 32, raw1);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            o0[i] = __float_as_uint(__uint_as_float(o0[i]) * alpha);
-            o1[i] = __float_as_uint(__uint_as_float(o1[i]) * alpha);
+            s[i] = __uint_as_float(raw0[i]);
+            s[32 + i] = __uint_as_float(raw1[i]);
           }
-          tmem_st32(oaddr, o0);
-          tmem_st32(oaddr + 32, o1);
         }
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[kPFull]);
-    }
+        if (j >= it.full_tiles || !ok) {
+          const int lim = ok ? min(limit, it.kv_len - 1) - key0 : -1;
+#pragma unroll
+          for (int c = 0; c < kKeys; ++c)
+            if (c > lim) s[c] = -INFINITY;
+        }
+        float mx8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+#pragma unroll
+        for (int c = 8; c < kKeys; c += 16) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mx8[i] = max3(mx8[i], s[c + i], s[c + 8 + i]);
+        }
+        const float mx = max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+        const float m_tile = mx * sl2;
+        // Rescale only when the row max grew by more than 2^8 (or on the
+        // first finite max); otherwise keep scaling by the stale max.
+        float alpha = 1.0f;
+        if (m_tile > m_used + kRescaleLog2) {
+          alpha = fast_exp2(m_used - m_tile);  // 0 when m_used = -inf
+          m_used = m_tile;
+        }
+        const float nm = m_used == -INFINITY ? 0.0f : -m_used;
+        float sum[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum[i] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < kKeys; c += 2) {
+          fma2(s[c], s[c + 1], s[c], s[c + 1], sl2, sl2, nm, nm);
+          if ((c & 15) == 14) {
+            exp2_fma_pair(s[c], s[c + 1]);  // one pair in eight on the FMA pipe
+          } else {
+            s[c] = fast_exp2(s[c]);
+            s[c + 1] = fast_exp2(s[c + 1]);
+          }
+          const int k = (c >> 1) & 3;  // four independent accumulator pairs
+          add2(sum[2 * k], sum[2 * k + 1], sum[2 * k], sum[2 * k + 1], s[c], s[c + 1]);
+        }
+        l = l * alpha + (((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7])));
 
-    // epilogue: O / l -> BF16 rows of `out`, natural-log LSE
-    if (alive && mbar_wait(&bars[kODone], (n_tiles - 1) & 1, kErrPrefillWait)) {
+        // P_g as packed BF16 pairs over the first 32 columns of S_g.
+        {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(s[2 * i], s[2 * i + 1]);
+          tmem_st32(trow + sb * kKeys, pk);
+        }
+        // One o_done phase per tile (PV_{g-1}); the item's first tile needs
+        // none: the previous epilogue consumed that phase.
+        if (j >= 1) {
+          if (!mbar_wait(&bars[kODone], (g - 1) & 1, kErrPrefillWait)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        // V rows that are not real keys (past kv_len, or an invalid page) are
+        // zeroed so that P = 0 never meets a non-finite cache value. All PVs
+        // before g are complete here, so this vfull wait is for V_g itself.
+        const int real_keys = ok ? min(kKeys, it.kv_len - key0) : 0;
+        if (real_keys < kKeys) {
+          const int st = g % kStages;
+          if (!mbar_wait(&bars[kVFull + st], (g / kStages) & 1, kErrPrefillWait)) {
+            alive = false;
+            break;
+          }
+          if (r < kKeys && r >= real_keys) {
+            const uint32_t vrow = sbase + kVOff + st * kKVBytes + r * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              st_shared_zero16(vrow + c * 16);
+              st_shared_zero16(vrow + kKVHalf + c * 16);
+            }
+          }
+          fence_proxy_async_smem();
+        }
+        if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t o0[32], o1[32];
+            const uint32_t oaddr = trow + kOCol + half * 64;
+            tmem_ld32(oaddr, o0);
+            tmem_ld32(oaddr + 32, o1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              o0[i] = __float_as_uint(__uint_as_float(o0[i]) * alpha);
+              o1[i] = __float_as_uint(__uint_as_float(o1[i]) * alpha);
+            }
+            tmem_st32(oaddr, o0);
+            tmem_st32(oaddr + 32, o1);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kPFull]);
+      }
+      if (!alive) break;
+
+      // epilogue: O / l -> BF16 rows of `out`, natural-log LSE; then O is free
+      const int g_last = gt + it.n_tiles - 1;
+      if (!mbar_wait(&bars[kODone], g_last & 1, kErrPrefillWait)) break;
       tc_fence_after();
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-      const int head = h * p.group + (r % p.group);
-      const long long tok = (long long)q_begin + q0 + rq;
       __nv_bfloat16* dst = p.out + (tok * p.qh + head) * 128;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -545,22 +590,26 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_ld_wait();
         if (valid_row) {
 #pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            const uint32_t* src = v < 4 ? o0 + 8 * v : o1 + 8 * (v - 4);
+          for (int vv = 0; vv < 8; ++vv) {
+            const uint32_t* src = vv < 4 ? o0 + 8 * vv : o1 + 8 * (vv - 4);
             uint4 w;
             w.x = pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
             w.y = pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
             w.z = pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
             w.w = pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
-            *reinterpret_cast<uint4*>(dst + half * 64 + v * 8) = w;
+            *reinterpret_cast<uint4*>(dst + half * 64 + vv * 8) = w;
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kOFree]);
       if (valid_row && p.lse) {
         const float m_out = m_used == -INFINITY ? 0.0f : m_used;
-        p.lse[((long long)b * p.qh + head) * p.max_q + q0 + rq] =
+        p.lse[((long long)it.b * p.qh + head) * p.max_q + it.q0 + rq] =
             l > 0.0f ? (m_out + fast_log2(l)) * kLn2 : -INFINITY;
       }
+      gt += it.n_tiles;
     }
   }
 
@@ -624,7 +673,17 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
-  const dim3 grid((a.max_q + qt - 1) / qt, a.batch, a.kvh);
+  static int sm_count[64] = {};
+  if (!sm_count[dev & 63]) {
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    sm_count[dev & 63] = n;
+  }
+  p.n_qtiles = (a.max_q + qt - 1) / qt;
+  const long long items = (long long)p.n_qtiles * a.batch * a.kvh;
+  if (items > 0x7fffffffLL) return cudaErrorNotSupported;
+  const int grid = int(items < 2LL * sm_count[dev & 63] ? items : 2LL * sm_count[dev & 63]);
   prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p, *qmap, *kmap, *vmap);
   return cudaGetLastError();
 }
