@@ -8,77 +8,97 @@
 // reference's: query i of a q_len-query group sees keys
 // [0, kv_len - q_len + i] (src/model.rs:1170-1188, smoke.cu:58).
 //
-// One CTA handles one 128-row query tile of one (sequence, kv head). Rows pack
-// the GQA group: row r = (query q0 + r / G, head h*G + r % G), so each K/V
-// tile loaded from HBM serves all G query heads. Per 64-key KV tile j:
+// Work item: one 128-row query tile of one (sequence, kv head). Rows pack the
+// GQA group: row r is (query q0 + r / G, head h*G + r % G), so each K/V tile
+// serves every query head of the group. Per 128-key KV tile t:
 //
-//   S_j = Q K_j^T   tcgen05.mma kind::f16, M=128 N=64 K=128 (8 x K16), A and
-//                   B from 128B-swizzled shared memory, D in TMEM (FP32)
-//   P_j = exp2(S_j * scale*log2e - m)   4 softmax warps, one TMEM lane (row)
-//                   per thread, written back over S_j in TMEM as packed BF16
-//   O  += P_j V_j   tcgen05.mma M=128 N=128 K=64 with A (P) read from TMEM,
-//                   V as an MN-major B operand from shared memory, O in TMEM
+//   S_t = Q K_t^T   tcgen05.mma kind::f16, M=128 N=128 K=128 (8 x K16), A and B
+//                   from 128B-swizzled shared memory, D in TMEM (FP32)
+//   P_t = exp2(S_t * scale*log2e - m)   two softmax warpgroups, each thread
+//                   one row and one half (64 keys) of the tile; P written back
+//                   over S_t in TMEM as packed BF16
+//   O  += P_t V_t   tcgen05.mma M=128 N=128 K=128, A (P) read from TMEM, V an
+//                   MN-major B operand in shared memory, O in TMEM
 //
-// Warp roles: warp 0 issues TMA (Q once, then a 2-stage K ring and a 2-stage V
-// ring over the sequence's pages: 3-D tensor maps over [tokens, kv_heads,
-// 128] with 64-element, 128-byte-swizzled boxes; a 64-key tile never crosses
-// a page since block_size is a multiple of 256); warp 1 owns TMEM (256
-// columns: S double buffer at 0 and 64, O at 128) and one thread issues the
-// MMAs and tcgen05.commit arrivals; warps 2..5 run the online softmax, the O
-// rescale (TMEM ld/st) and the epilogue. S/P is double-buffered in TMEM and
-// a buffer is released by the commit of the PV MMA that read its P; the
-// softmax of tile j computes and stores P_j before it waits for PV_{j-1}.
+// S/P is triple-buffered in TMEM (columns 0, 128, 256; O at 384): S_{t+1} is
+// issued as soon as PV_{t-2} has released its buffer, so the tensor core
+// computes the next scores while the softmax works on the current ones and
+// the per-tile work of the tensor core (1024 cycles at M=N=K=128) overlaps the
+// softmax (~1000-1300 cycles, bounded by the 16-per-clock MUFU unit).
 //
-// Sizing for B200: 96 KB of tiles + 1 KB of barriers per CTA and 256 TMEM
-// columns let two CTAs share an SM (2 x 256 of the 512 columns), so one CTA's
-// softmax runs while the other's MMAs use the tensor core, and their
-// prologues/epilogues overlap. The softmax uses Blackwell's packed FP32x2
-// FMA/ADD and three-input max to cut its instruction count, and evaluates an
-// eighth of the exponentials on the FMA pipe (exp2_fma) next to the
-// 16-per-clock MUFU unit.
+// Roles (16 warps, one CTA per SM):
+//   warp 0      claims items (global counter, heaviest first), publishes each
+//               to the CTA through a two-slot ring, loads Q (two buffers) and
+//               the K tiles (two-stage ring) with TMA: 3-D maps over [tokens,
+//               kv_heads, 128], 64-element 128-byte-swizzled boxes; a 128-key
+//               tile never crosses a page since block_size is a multiple of 256
+//   warp 1      TMEM owner; one thread issues every MMA and commit
+//   warp 2      V fixer: zeroes V rows that are not real keys (past kv_len or an
+//               invalid page) so P ~ 0 never meets a non-finite cache value,
+//               then releases the tile to the MMA
+//   warp 3      loads the V tiles (two-stage ring)
+//   warps 4-7   softmax of keys 0-63 of each tile; warps 8-11 keys 64-127. The
+//               two halves of a row agree on its max through shared memory and
+//               a per-quadrant mbarrier (no bar.sync: every wait is bounded)
+//   warps 12-15 epilogue: O / l -> BF16 rows and the LSE, from row statistics
+//               handed over in shared memory; frees O for the next item
 //
-// The kernel is persistent: 2 CTAs per SM loop over (query tile, sequence,
-// kv head) items, longest causal tiles first, keeping their barriers and
-// TMEM; the next item's Q load and first K/V tiles overlap the current
-// item's last tiles and epilogue. Barrier phases are tracked with global
-// tile and item counters; q_free (all S MMAs of an item done) and o_free (its
-// epilogue has read O) guard the two buffers reused across items. The softmax keeps the
-// running max it scales by unless a row's max grows by more than 2^8
-// (FA4-style lazy rescale: P stays <= 256, exact after the final divide), so
-// the TMEM read-modify-write of O is rare after the first tiles.
+// The softmax keeps the running max it scales by unless a row's max grows by
+// more than 2^8 (lazy rescale: P stays <= 256, exact after the final divide),
+// so the TMEM read-modify-write of O is rare. An eighth of the exponentials
+// run on the FMA pipe (exp2_fma_pair).
 //
-// Every wait is bounded (common.cuh); a timeout records an error code and the
-// CTA still frees its TMEM and exits.
+// mbarrier parity waits are sound only if a waiter is never two phases
+// behind or ahead of the barrier; every barrier below is waited at every
+// phase, in order, by each role that waits on it, and its next phase needs
+// that role's progress. Every wait is bounded (common.cuh); a timeout records
+// an error code, the CTA drains its in-flight copies and MMAs (bounded), frees
+// TMEM and exits.
+#include <mutex>
+
 #include "internal.cuh"
 
 namespace nvb {
 
 namespace prefill_detail {
 
-constexpr int kRows = 128;
-constexpr int kKeys = 64;
-constexpr int kStages = 2;
-constexpr int kQHalf = kRows * 128;          // 128 rows x 64 BF16 (one 128-byte swizzle column)
-constexpr int kQBytes = 2 * kQHalf;          // Q tile 128 x 128 BF16
-constexpr int kKVHalf = kKeys * 128;         // 64 keys x 64 BF16
-constexpr int kKVBytes = 2 * kKVHalf;        // K or V tile 64 x 128 BF16
-constexpr int kThreads = 192;
-constexpr int kTmemCols = 256;
-constexpr int kOCol = 128;
+constexpr int kRows = 128;                   // query rows per item (TMEM lanes)
+constexpr int kKeys = 128;                   // keys per KV tile
+constexpr int kHalf = 128 * 128;             // 128 rows x 64 BF16 (one 128-byte swizzle column)
+constexpr int kQBytes = 2 * kHalf;           // Q tile 128 x 128 BF16
+constexpr int kKVBytes = 2 * kHalf;          // K or V tile 128 x 128 BF16
+constexpr int kQStages = 2, kKStages = 2, kVStages = 2;
+constexpr int kSBufs = 3;                    // S/P buffers in TMEM
+constexpr int kThreads = 512;
+constexpr int kTmemCols = 512;
+constexpr int kOCol = 384;
 constexpr float kLn2 = 0.693147180559945309f;
 constexpr float kRescaleLog2 = 8.0f;         // lazy rescale threshold (P <= 2^8)
 
-// Barriers and the TMEM slot sit below the first 1024-byte boundary; the
-// tiles follow on 1024-byte boundaries (128-byte swizzle atoms).
-enum Bar { kQFull = 0, kKFull = 1, kKEmpty = 3, kVFull = 5, kVEmpty = 7, kSFull = 9, kSFree = 11, kPFull = 13,
-           kODone = 14, kQFree = 15, kOFree = 16, kNumBars = 17 };
+enum Bar {
+  kQFull = 0, kQFree = 2, kKFull = 4, kKEmpty = 6, kVFull = 8, kVFixed = 10, kVEmpty = 12,  // [2]
+  kSFull = 14, kPVDone = 17,                                                               // [3]: per S buffer
+  kPFull = 20, kODone = 21, kOFree = 22, kStatsFull = 23, kStatsFree = 24,
+  kXchg = 25,                                                                              // [4]: per TMEM quadrant
+  kItemFull = 29, kItemEmpty = 31,                                                         // [2]
+  kDrain = 33, kNumBars = 34
+};
+// Readers of each published item: V producer, MMA issuer, V fixer (one
+// arrival each) and the 8 softmax + 4 epilogue warps (one per warp).
+constexpr int kItemReaders = 15;
 constexpr int kTmemSlotOff = kNumBars * 8;
-constexpr int kHeadBytes = kTmemSlotOff + 16;
-constexpr int kQOff = 0;                      // offsets from the aligned tile base
-constexpr int kKOff = kQOff + kQBytes;
-constexpr int kVOff = kKOff + kStages * kKVBytes;
-constexpr int kTileBytes = kVOff + kStages * kKVBytes;  // 96 KB
-constexpr int kSmemBytes = 1024 + kTileBytes;           // 97 KB: two CTAs per SM
+constexpr int kItemOff = 320;                               // Item [2] (the published-item ring)
+constexpr int kItemBytes = 64;
+constexpr int kStatsOff = 512;                              // float2 [128]: row max used, row sum
+constexpr int kXOff = kStatsOff + kRows * 8;                // float [2 slots][2 halves][128]
+constexpr int kHeadBytes = kXOff + 2 * 2 * kRows * 4;
+constexpr int kQOff = 0;                                    // offsets from the 1 KB aligned tile base
+constexpr int kKOff = kQOff + kQStages * kQBytes;
+constexpr int kVOff = kKOff + kKStages * kKVBytes;
+constexpr int kTileBytes = kVOff + kVStages * kKVBytes;     // 192 KB
+constexpr int kSmemBytes = kTileBytes + kHeadBytes + 1024;  // + worst-case alignment pad
+static_assert(kTmemSlotOff + 4 <= kItemOff && kItemOff + 2 * kItemBytes <= kStatsOff, "head layout overlaps");
+static_assert(kSmemBytes <= 232448, "tile layout exceeds the per-CTA shared memory limit");
 
 struct PrefillParams {
   int n_qtiles;  // query tiles of the longest sequence
@@ -89,6 +109,7 @@ struct PrefillParams {
   float* lse;
   int batch, max_q, qh, kvh, group, qt, rows_used, block_size, table_stride, num_blocks;
   float scale_log2;
+  int* sched;  // {next item to claim, CTAs finished}: zero at launch, reset by the last CTA
 };
 
 // ------------------------------------------------------------- tcgen05 PTX
@@ -104,11 +125,11 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uin
 }
 
 // Instruction descriptors, kind::f16: FP32 accumulator, BF16 A and B, A
-// K-major, M = 128. S = Q K^T: B K-major, N = 64 keys. O += P V: B MN-major,
-// N = 128 head dims.
-constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 4) << 24);
-constexpr uint32_t kIdescS = kIdescBase | ((uint32_t(kKeys) >> 3) << 17);
-constexpr uint32_t kIdescPV = kIdescBase | (1u << 16) | ((128u >> 3) << 17);
+// K-major, M = 128, N = 128. S = Q K^T: B K-major (keys). O += P V: B
+// MN-major (head dims contiguous).
+constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 4) << 24) | ((128u >> 3) << 17);
+constexpr uint32_t kIdescS = kIdescBase;
+constexpr uint32_t kIdescPV = kIdescBase | (1u << 16);
 
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
@@ -116,11 +137,6 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t 
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
 }
 
 // O += P V with A (P, packed BF16 pairs) read from tensor memory.
@@ -133,24 +149,9 @@ __device__ __forceinline__ void umma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tme
       : "memory");
 }
 
-// 2^x on the FMA/ALU pipes for x <= 128 (used for part of the softmax so the
-// MUFU unit is not the limit). Range reduction x = n + f with n the nearest
-// integer (1.5 * 2^23 rounding trick, |f| <= 1/2), then a degree-4
-// polynomial for 2^f fitted to minimise relative error on [-1/2, 1/2] (this
-// file's own fit; max relative error 2.7e-6 in FP32), then n is added to the
-// exponent field. Inputs below -125 (masked keys are -inf) return exactly 0;
-// the clamp keeps the exponent add from leaving the normal range.
-__device__ __forceinline__ float exp2_fma(float x) {
-  const float xc = fmaxf(x, -125.0f);
-  const float t = xc + 12582912.0f;  // 1.5 * 2^23: low mantissa bits hold round(xc)
-  const float f = xc - (t - 12582912.0f);
-  float p = 0.009570096619427204f;
-  p = fmaf(p, f, 0.05591785907745361f);
-  p = fmaf(p, f, 0.240247443318367f);
-  p = fmaf(p, f, 0.6931217908859253f);
-  p = fmaf(p, f, 0.9999992847442627f);
-  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-  return x < -125.0f ? 0.0f : r;
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
 }
 
 // Packed FP32 pairs (Blackwell f32x2 ALU forms): d = a * b + c, d = a + b.
@@ -177,7 +178,14 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
-// exp2_fma on a pair of inputs with the packed FP32 forms.
+// 2^x for a pair of inputs on the FMA pipe (x <= 128), for a share of the
+// softmax beside the 16-per-clock MUFU unit. Range reduction x = n + f with
+// n the nearest integer (1.5 * 2^23 rounding trick, |f| <= 1/2), a degree-4
+// polynomial for 2^f fitted to minimise relative error on [-1/2, 1/2] (this
+// file's own fit; max relative error 2.7e-6 in FP32), then n added to the
+// exponent field with one integer multiply-add. Inputs are clamped at -125,
+// so a masked key (-inf) gives 2^-125 rather than 0: ~1e-38 of a value that
+// the caller's V zeroing or row statistics make irrelevant.
 __device__ __forceinline__ void exp2_fma_pair(float& a, float& b) {
   const float xa = fmaxf(a, -125.0f), xb = fmaxf(b, -125.0f);
   float ta, tb, na, nb, fa, fb, pa, pb;
@@ -188,10 +196,8 @@ __device__ __forceinline__ void exp2_fma_pair(float& a, float& b) {
   fma2(pa, pb, pa, pb, fa, fb, 0.240247443318367f, 0.240247443318367f);
   fma2(pa, pb, pa, pb, fa, fb, 0.6931217908859253f, 0.6931217908859253f);
   fma2(pa, pb, pa, pb, fa, fb, 0.9999992847442627f, 0.9999992847442627f);
-  const float ra = __int_as_float(__float_as_int(pa) + (__float_as_int(ta) << 23));
-  const float rb = __int_as_float(__float_as_int(pb) + (__float_as_int(tb) << 23));
-  a = a < -125.0f ? 0.0f : ra;
-  b = b < -125.0f ? 0.0f : rb;
+  a = __int_as_float(__float_as_int(ta) * 8388608 + __float_as_int(pa));  // exponent += round(x)
+  b = __int_as_float(__float_as_int(tb) * 8388608 + __float_as_int(pb));
 }
 
 #define NVB_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), \
@@ -216,6 +222,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      NVB_W8(0), NVB_W8(8)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -223,80 +237,115 @@ __device__ __forceinline__ void st_shared_zero16(uint32_t addr) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0) : "memory");
 }
 
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
-               : "memory");
-}
-
 __device__ __forceinline__ bool page_ok(int page, int num_blocks) { return page >= 0 && page < num_blocks; }
 
-// One query tile of one (sequence, kv head): the work item of the
-// persistent loop. Virtual items are ordered by query-tile index, longest
-// causal tiles first, and dealt round-robin to the CTAs.
+
+// Every lane of the warp waits; the warp continues only if all of them saw
+// the phase complete, so a timeout never splits the warp before the
+// .sync.aligned TMEM instructions that follow.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, kErrPrefillWait));
+}
+
+// One 128-row query tile of one (sequence, kv head): the work item of the
+// persistent loop. Virtual items are grouped by (sequence, kv head), longest
+// causal tile first within a group, so the CTAs running at one time share a
+// few groups' K/V in L2; CTAs claim items from a global counter (dynamic load
+// balancing), so an SM that drew short items takes more of them.
 struct Item {
-  int b, h, q_begin, q_len, q0, qt_eff, kv_len, prefix, key_end, n_tiles, full_tiles;
-  bool empty;
+  int b, h, q_begin, q0, kv_len, prefix;
+  int qx;       // queries in the tile
+  int key_end;  // keys its last query sees
+  int n;        // KV tiles it visits
+  int full;     // leading KV tiles that every row sees whole
 };
+static_assert(sizeof(Item) <= kItemBytes, "item ring slot too small");
 
 __device__ __forceinline__ Item make_item(const PrefillParams& p, int v) {
   Item it;
-  const int pairs = p.batch * p.kvh;
-  const int tile = p.n_qtiles - 1 - v / pairs;
-  const int rest = v % pairs;
-  it.b = rest / p.kvh;
-  it.h = rest % p.kvh;
+  const int group = v / p.n_qtiles;
+  const int tile = p.n_qtiles - 1 - (v - group * p.n_qtiles);
+  it.b = group / p.kvh;
+  it.h = group - it.b * p.kvh;
   it.q_begin = p.cu_q[it.b];
-  it.q_len = p.cu_q[it.b + 1] - it.q_begin;
+  const int q_len = p.cu_q[it.b + 1] - it.q_begin;
   it.q0 = tile * p.qt;
-  it.empty = it.q0 >= it.q_len;
-  it.qt_eff = it.empty ? 0 : min(p.qt, it.q_len - it.q0);
-  it.kv_len = it.empty ? 0 : p.kv_lens[it.b];
-  it.prefix = it.kv_len - it.q_len;
+  it.qx = max(0, min(p.qt, q_len - it.q0));
+  it.kv_len = it.qx > 0 ? p.kv_lens[it.b] : 0;
+  it.prefix = it.kv_len - q_len;
   // A context longer than the page table, or shorter than its query group,
   // is invalid input: such rows get zero output (as decode does).
-  const bool seq_ok = !it.empty && it.prefix >= 0 &&
-                      (long long)it.kv_len <= (long long)p.table_stride * p.block_size;
-  it.key_end = seq_ok ? min(it.kv_len, it.prefix + it.q0 + it.qt_eff) : 0;
-  it.n_tiles = it.key_end > 0 ? (it.key_end + kKeys - 1) / kKeys : 0;
-  const int free_keys = min(it.kv_len, it.prefix + it.q0 + 1);  // keys every row of the tile sees
-  it.full_tiles = free_keys > 0 ? free_keys / kKeys : 0;
+  const bool seq_ok = it.qx > 0 && it.prefix >= 0 && (long long)it.kv_len <= (long long)p.table_stride * p.block_size;
+  it.key_end = seq_ok ? min(it.kv_len, it.prefix + it.q0 + it.qx) : 0;
+  it.n = (it.key_end + kKeys - 1) / kKeys;
+  it.full = seq_ok ? min(it.kv_len, it.prefix + it.q0 + 1) / kKeys : 0;
   return it;
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+// Item i of this CTA from the two-slot ring the scheduler publishes.
+// `warp_level`: every lane reads it and lane 0 arrives for the warp.
+// Returns false at the end marker (b < 0) or if the wait gave up.
+__device__ __forceinline__ bool take_item(uint64_t* bars, const Item* ring, int i, bool warp_level, Item& it) {
+  const int slot = i & 1;
+  const uint32_t par = (i >> 1) & 1;
+  if (warp_level) {
+    if (!warp_wait(&bars[kItemFull + slot], par)) return false;
+  } else if (!mbar_wait(&bars[kItemFull + slot], par, kErrPrefillWait)) {
+    return false;
+  }
+  it = ring[slot];
+  if (warp_level) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&bars[kItemEmpty + slot]);
+  } else {
+    mbar_arrive(&bars[kItemEmpty + slot]);
+  }
+  return it.b >= 0;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
                    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
-  // tiles start at the first 1024-byte boundary past the barrier block
-  const uint32_t tile_addr = (raw_addr + kHeadBytes + 1023u) & ~1023u;
-  unsigned char* tiles = smem_raw + (tile_addr - raw_addr);
-  const uint32_t sbase = tile_addr;
-  if (tile_addr + kTileBytes > raw_addr + kSmemBytes) {  // dynamic smem base not 1 KB friendly
-    if (threadIdx.x == 0) record_error(kErrPrefillAlign);
-    return;
-  }
+  // tiles start at the first 1024-byte boundary; the head block follows
+  const uint32_t sbase = (raw_addr + 1023u) & ~1023u;
+  unsigned char* tiles = smem_raw + (sbase - raw_addr);
+  unsigned char* head = tiles + kTileBytes;
   const int n_items = p.n_qtiles * p.batch * p.kvh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + kTmemSlotOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(head);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(head + kTmemSlotOff);
+  Item* ring = reinterpret_cast<Item*>(head + kItemOff);
+  float2* stats = reinterpret_cast<float2*>(head + kStatsOff);
+  float* xch = reinterpret_cast<float*>(head + kXOff);
   if (threadIdx.x == 0) {
-    mbar_init(&bars[kQFull], 1);
-    mbar_init(&bars[kQFree], 1);
-    mbar_init(&bars[kOFree], 4);
-    for (int s = 0; s < kStages; ++s) {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[kQFull + s], 1);
+      mbar_init(&bars[kQFree + s], 1);
       mbar_init(&bars[kKFull + s], 1);
       mbar_init(&bars[kKEmpty + s], 1);
       mbar_init(&bars[kVFull + s], 1);
+      mbar_init(&bars[kVFixed + s], 1);
       mbar_init(&bars[kVEmpty + s], 1);
+      mbar_init(&bars[kItemFull + s], 1);
+      mbar_init(&bars[kItemEmpty + s], kItemReaders);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars[kSFull + s], 1);
-      mbar_init(&bars[kSFree + s], 1);
+#pragma unroll
+    for (int b = 0; b < kSBufs; ++b) {
+      mbar_init(&bars[kSFull + b], 1);
+      mbar_init(&bars[kPVDone + b], 1);
     }
-    mbar_init(&bars[kPFull], 4);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mbar_init(&bars[kXchg + q], 64);
+    mbar_init(&bars[kPFull], 8);
     mbar_init(&bars[kODone], 1);
+    mbar_init(&bars[kOFree], 4);
+    mbar_init(&bars[kStatsFull], kRows);
+    mbar_init(&bars[kStatsFree], kRows);
+    mbar_init(&bars[kDrain], 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -305,12 +354,14 @@ __global__ void __launch_bounds__(kThreads, 2)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (warp >= 2 && p.rows_used < kRows) {
+  if (warp >= 12 && p.rows_used < kRows) {
     // Rows past the packed (query, head) rows are never loaded: zero them once.
-    const int t = threadIdx.x - 64;
-    for (int e = t; e < (kRows - p.rows_used) * 16; e += 128) {
-      const int r = p.rows_used + (e >> 4), c = e & 15;
-      st_shared_zero16(sbase + kQOff + (c >> 3) * kQHalf + r * 128 + (c & 7) * 16);
+    const int t = threadIdx.x - 384;
+    const int per = (kRows - p.rows_used) * 16;  // 16-byte chunks per Q buffer
+    for (int e = t; e < kQStages * per; e += 128) {
+      const int s = e / per, rem = e - s * per;
+      const int r = p.rows_used + (rem >> 4), c = rem & 15;
+      st_shared_zero16(sbase + kQOff + s * kQBytes + (c >> 3) * kHalf + r * 128 + (c & 7) * 16);
     }
     fence_proxy_async_smem();
   }
@@ -320,179 +371,287 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // -------------------------------------------------------- TMA producer
+    // ------------------------------------- scheduler, Q and K producer
     if (lane == 0) {
       tma_prefetch_desc(&qmap);
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      int gt = 0, it_count = 0;
+      int gt = 0, ix = 0, k_issued = 0;
       bool alive = true;
-      for (int v = blockIdx.x; v < n_items && alive; v += gridDim.x) {
-        const Item it = make_item(p, v);
-        if (it.n_tiles == 0) continue;
+      for (int i = 0; alive; ++i) {
+        // claim the next item that has queries
+        int v;
+        Item it;
+        do {
+          v = atomicAdd(p.sched, 1);
+          if (v >= n_items) break;
+          it = make_item(p, v);
+          if (it.qx == 0) {
+            // Tiles past the sequence's queries come first in their group:
+            // move the counter to the group's last (non-empty) tile if nobody
+            // has claimed past this one yet.
+            const int q_len = p.cu_q[it.b + 1] - it.q_begin;
+            const int tiles = (q_len + p.qt - 1) / p.qt;
+            const int group_end = (v / p.n_qtiles + 1) * p.n_qtiles;
+            atomicCAS(p.sched, v + 1, group_end - tiles);
+          }
+        } while (it.qx == 0);
+        const bool end = v >= n_items;
+        if (end) it.b = -1;
+        if (i >= 2 && !mbar_wait(&bars[kItemEmpty + (i & 1)], ((i >> 1) + 1) & 1, kErrPrefillWait)) break;
+        ring[i & 1] = it;
+        mbar_arrive(&bars[kItemFull + (i & 1)]);
+        if (end) break;
+        if (it.n == 0) continue;  // rows without keys: only the epilogue acts
+        const int qs = ix & 1;
+        // Q buffer qs is free once the last S MMA of item ix-2 completed.
+        if (ix >= 2 && !mbar_wait(&bars[kQFree + qs], ((ix >> 1) + 1) & 1, kErrPrefillWait)) break;
+        mbar_arrive_expect_tx(&bars[kQFull + qs], 2u * 128u * uint32_t(p.rows_used));
+        {
+          const int qy = it.h * p.group, qz = it.q_begin + it.q0;
+          unsigned char* qdst = tiles + kQOff + qs * kQBytes;
+          tma_load_3d(qdst, &qmap, &bars[kQFull + qs], 0, qy, qz);
+          tma_load_3d(qdst + kHalf, &qmap, &bars[kQFull + qs], 64, qy, qz);
+        }
+        ++ix;
         const int* table = p.block_table + (long long)it.b * p.table_stride;
-        // Q of the previous item is free once all its S MMAs completed.
-        if (it_count > 0 && !mbar_wait(&bars[kQFree], (it_count - 1) & 1, kErrPrefillWait)) break;
-        mbar_arrive_expect_tx(&bars[kQFull], 2u * 128u * uint32_t(p.rows_used));
-        const int qy = it.h * p.group, qz = it.q_begin + it.q0;
-        tma_load_3d(tiles + kQOff, &qmap, &bars[kQFull], 0, qy, qz);
-        tma_load_3d(tiles + kQOff + kQHalf, &qmap, &bars[kQFull], 64, qy, qz);
-        for (int j = 0; j < it.n_tiles; ++j) {
-          const int g = gt + j;
-          const int st = g % kStages;
-          const uint32_t par = ((g / kStages) + 1) & 1;
+        for (int j = 0; j < it.n; ++j) {
+          const int g = gt + j, st = g & 1;
           const int key0 = j * kKeys;
           const int logical = key0 / p.block_size;
           const int page = table[logical];
           const bool ok = page_ok(page, p.num_blocks);
           const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
-          if (g >= kStages && !mbar_wait(&bars[kKEmpty + st], par, kErrPrefillWait)) { alive = false; break; }
+          if (g >= kKStages && !mbar_wait(&bars[kKEmpty + st], ((g >> 1) + 1) & 1, kErrPrefillWait)) {
+            alive = false;
+            break;
+          }
           unsigned char* kdst = tiles + kKOff + st * kKVBytes;
           if (ok) {
             mbar_arrive_expect_tx(&bars[kKFull + st], kKVBytes);
             tma_load_3d(kdst, &kmap, &bars[kKFull + st], 0, it.h, trow);
-            tma_load_3d(kdst + kKVHalf, &kmap, &bars[kKFull + st], 64, it.h, trow);
+            tma_load_3d(kdst + kHalf, &kmap, &bars[kKFull + st], 64, it.h, trow);
           } else {
             mbar_arrive(&bars[kKFull + st]);
           }
-          if (g >= kStages && !mbar_wait(&bars[kVEmpty + st], par, kErrPrefillWait)) { alive = false; break; }
+          k_issued = g + 1;
+        }
+        gt += it.n;
+      }
+      // Drain: every copy this thread issued has landed before the CTA exits
+      // (already true on the normal path; bounded on an error path).
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        if (k_issued > s) mbar_wait(&bars[kKFull + s], ((k_issued - 1 - s) >> 1) & 1, kErrPrefillWait);
+        if (ix > s) mbar_wait(&bars[kQFull + s], ((ix - 1 - s) >> 1) & 1, kErrPrefillWait);
+      }
+    }
+  } else if (warp == 3) {
+    // ------------------------------------------------------- V producer
+    if (lane == 0) {
+      tma_prefetch_desc(&vmap);
+      int gt = 0, v_issued = 0;
+      bool alive = true;
+      Item it;
+      for (int i = 0; alive && take_item(bars, ring, i, false, it); ++i) {
+        if (it.n == 0) continue;
+        const int* table = p.block_table + (long long)it.b * p.table_stride;
+        for (int j = 0; j < it.n; ++j) {
+          const int g = gt + j, st = g & 1;
+          const int key0 = j * kKeys;
+          const int logical = key0 / p.block_size;
+          const int page = table[logical];
+          const bool ok = page_ok(page, p.num_blocks);
+          const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
+          if (g >= kVStages && !mbar_wait(&bars[kVEmpty + st], ((g >> 1) + 1) & 1, kErrPrefillWait)) {
+            alive = false;
+            break;
+          }
           unsigned char* vdst = tiles + kVOff + st * kKVBytes;
           if (ok) {
             mbar_arrive_expect_tx(&bars[kVFull + st], kKVBytes);
             tma_load_3d(vdst, &vmap, &bars[kVFull + st], 0, it.h, trow);
-            tma_load_3d(vdst + kKVHalf, &vmap, &bars[kVFull + st], 64, it.h, trow);
+            tma_load_3d(vdst + kHalf, &vmap, &bars[kVFull + st], 64, it.h, trow);
           } else {
             mbar_arrive(&bars[kVFull + st]);
           }
+          v_issued = g + 1;
         }
-        gt += it.n_tiles;
-        ++it_count;
+        gt += it.n;
       }
+#pragma unroll
+      for (int s = 0; s < 2; ++s)
+        if (v_issued > s) mbar_wait(&bars[kVFull + s], ((v_issued - 1 - s) >> 1) & 1, kErrPrefillWait);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t q_addr = sbase + kQOff;
-      int gt = 0, it_count = 0;
+      int gt = 0, ix = 0;  // tiles and items (with keys) so far
       bool alive = true;
-      // PV for global tile g; `first` starts a new item's accumulator, which
-      // must wait until the previous item's epilogue has read O.
-      auto issue_pv = [&](int g, bool first) {
-        const int st = g % kStages;
-        if (first && it_count > 0) alive = alive && mbar_wait(&bars[kOFree], (it_count - 1) & 1, kErrPrefillWait);
-        alive = alive && mbar_wait(&bars[kPFull], g & 1, kErrPrefillWait);
-        alive = alive && mbar_wait(&bars[kVFull + st], (g / kStages) & 1, kErrPrefillWait);
-        if (!alive) return;
+      // O += P_t V_t. Waits for the fixer's V, the softmax's P and, for the
+      // item's first tile, the epilogue's read of the previous O.
+      auto issue_pv = [&](int t, bool first, bool last) -> bool {
+        const int vs = t & 1, buf = t % kSBufs;
+        if (!mbar_wait(&bars[kVFixed + vs], (t >> 1) & 1, kErrPrefillWait)) return false;
+        if (first && ix > 0 && !mbar_wait(&bars[kOFree], (ix - 1) & 1, kErrPrefillWait)) return false;
+        if (!mbar_wait(&bars[kPFull], t & 1, kErrPrefillWait)) return false;
         tc_fence_after();
-        const uint32_t v_addr = sbase + kVOff + st * kKVBytes;
-        const uint32_t p_tmem = tmem + (g & 1) * kKeys;  // P_g over S_g: 16 keys = 8 columns
+        const uint32_t v_addr = sbase + kVOff + vs * kKVBytes;
 #pragma unroll
-        for (int kk = 0; kk < kKeys / 16; ++kk) {
-          const uint64_t bd = sw128_desc(v_addr + kk * 2048, kKVHalf, 1024);
-          umma_bf16_tmem_a(tmem + kOCol, p_tmem + kk * 8, bd, kIdescPV, (!first || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) {
+          // P: 16 keys = 8 packed columns; V: 16 keys = 2048 bytes of rows
+          umma_bf16_tmem_a(tmem + kOCol, tmem + buf * kKeys + kk * 8, sw128_desc(v_addr + kk * 2048, kHalf, 1024),
+                           kIdescPV, (!first || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bars[kVEmpty + st]);
-        umma_commit(&bars[kODone]);
-        umma_commit(&bars[kSFree + (g & 1)]);  // S/P buffer free once PV_g has read P_g
+        umma_commit(&bars[kPVDone + buf]);
+        umma_commit(&bars[kVEmpty + vs]);
+        if (last) umma_commit(&bars[kODone]);
+        return true;
       };
-      for (int v = blockIdx.x; v < n_items && alive; v += gridDim.x) {
-        const Item it = make_item(p, v);
-        if (it.n_tiles == 0) continue;
-        alive = mbar_wait(&bars[kQFull], it_count & 1, kErrPrefillWait);
-        tc_fence_after();
-        for (int j = 0; j < it.n_tiles && alive; ++j) {
-          const int g = gt + j;
-          const int st = g % kStages, sb = g & 1;
-          alive = mbar_wait(&bars[kKFull + st], (g / kStages) & 1, kErrPrefillWait);
-          if (alive && g >= 2) alive = mbar_wait(&bars[kSFree + sb], ((g >> 1) + 1) & 1, kErrPrefillWait);
+      Item it;
+      for (int i = 0; alive && take_item(bars, ring, i, false, it); ++i) {
+        if (it.n == 0) continue;
+        const int qs = ix & 1;
+        const uint32_t q_addr = sbase + kQOff + qs * kQBytes;
+        for (int j = 0; j < it.n && alive; ++j) {
+          const int t = gt + j, ks = t & 1, buf = t % kSBufs;
+          alive = mbar_wait(&bars[kKFull + ks], (t >> 1) & 1, kErrPrefillWait);
+          if (alive && j == 0) alive = mbar_wait(&bars[kQFull + qs], (ix >> 1) & 1, kErrPrefillWait);
+          // buffer `buf` last held P_{t-3}: PV_{t-3} must have read it
+          if (alive && t >= kSBufs)
+            alive = mbar_wait(&bars[kPVDone + buf], ((t - kSBufs) / kSBufs) & 1, kErrPrefillWait);
           if (!alive) break;
           tc_fence_after();
-          const uint32_t k_addr = sbase + kKOff + st * kKVBytes;
+          const uint32_t k_addr = sbase + kKOff + ks * kKVBytes;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
-            const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-            umma_bf16(tmem + sb * kKeys, sw128_desc(q_addr + qoff, 16, 1024), sw128_desc(k_addr + koff, 16, 1024),
+            const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+            umma_bf16(tmem + buf * kKeys, sw128_desc(q_addr + off, 16, 1024), sw128_desc(k_addr + off, 16, 1024),
                       kIdescS, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&bars[kKEmpty + st]);
-          umma_commit(&bars[kSFull + sb]);
-          if (j >= 1) issue_pv(g - 1, j == 1);
+          umma_commit(&bars[kSFull + buf]);
+          umma_commit(&bars[kKEmpty + ks]);
+          if (j == it.n - 1) umma_commit(&bars[kQFree + qs]);
+          if (j >= 1) alive = issue_pv(t - 1, j == 1, false);
         }
+        if (alive) alive = issue_pv(gt + it.n - 1, it.n == 1, true);
         if (!alive) break;
-        umma_commit(&bars[kQFree]);  // every S MMA of this item has been issued
-        issue_pv(gt + it.n_tiles - 1, it.n_tiles == 1);
-        gt += it.n_tiles;
-        ++it_count;
+        ++ix;
+        gt += it.n;
       }
+      // every MMA issued by this thread completes before TMEM is freed
+      umma_commit(&bars[kDrain]);
+      mbar_wait(&bars[kDrain], 0, kErrPrefillWait);
     }
-  } else {
-    // ---------------------------------------------- softmax and epilogue
-    const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // TMEM lane = packed row
-    const uint32_t trow = tmem + (uint32_t(quad * 32) << 16);
-    const int rq = r / p.group;
-    const float sl2 = p.scale_log2;
+  } else if (warp == 2) {
+    // ---------------------------------------------------------- V fixer
     int gt = 0;
     bool alive = true;
-    for (int v = blockIdx.x; v < n_items && alive; v += gridDim.x) {
-      const Item it = make_item(p, v);
-      if (it.empty) continue;
-      const int head = it.h * p.group + (r % p.group);
-      const bool valid_row = r < p.rows_used && rq < it.qt_eff;
-      const long long tok = (long long)it.q_begin + it.q0 + rq;
-      if (it.n_tiles == 0) {
-        // No visible keys (invalid context): zero rows, -inf LSE.
-        if (valid_row) {
-          __nv_bfloat16* dst = p.out + (tok * p.qh + head) * 128;
-          for (int d = 0; d < 128; d += 8) *reinterpret_cast<uint4*>(dst + d) = make_uint4(0, 0, 0, 0);
-          if (p.lse) p.lse[((long long)it.b * p.qh + head) * p.max_q + it.q0 + rq] = -INFINITY;
-        }
-        continue;
-      }
+    Item it;
+    for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
+      if (it.n == 0) continue;
       const int* table = p.block_table + (long long)it.b * p.table_stride;
-      const int limit = valid_row ? it.prefix + it.q0 + rq : it.key_end - 1;  // last visible key
-      float m_used = -INFINITY, l = 0.0f;  // running max the probabilities are scaled by
-      for (int j = 0; j < it.n_tiles; ++j) {
-        const int g = gt + j;
-        const int sb = g & 1;
+      for (int j = 0; j < it.n; ++j) {
+        const int g = gt + j, st = g & 1;
         const int key0 = j * kKeys;
         const bool ok = page_ok(table[key0 / p.block_size], p.num_blocks);
-        if (!mbar_wait(&bars[kSFull + sb], (g >> 1) & 1, kErrPrefillWait)) {
+        const int real = ok ? min(kKeys, it.kv_len - key0) : 0;
+        if (!warp_wait(&bars[kVFull + st], (g >> 1) & 1)) {
+          alive = false;
+          break;
+        }
+        if (real < kKeys) {
+          const uint32_t vbase = sbase + kVOff + st * kKVBytes;
+          for (int e = lane; e < (kKeys - real) * 16; e += 32) {
+            const int row = real + (e >> 4), c = e & 15;
+            st_shared_zero16(vbase + (c >> 3) * kHalf + row * 128 + (c & 7) * 16);
+          }
+          fence_proxy_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kVFixed + st]);
+      }
+      gt += it.n;
+    }
+  } else if (warp < 12) {
+    // ---------------------------------------------------------- softmax
+    const int hf = (warp - 4) >> 2;  // which 64 keys of each tile
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // TMEM lane = packed row
+    const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
+    const int rq = r / p.group;
+    const float sl2 = p.scale_log2;
+    int t = 0, ix = 0, xc = 0;  // tiles, items with keys, max exchanges
+    bool alive = true;
+    // Exchange one value per row with the other half (same TMEM quadrant).
+    auto exchange = [&](float mine, float& other) -> bool {
+      float* slot = xch + (xc & 1) * 2 * kRows;
+      slot[hf * kRows + r] = mine;
+      mbar_arrive(&bars[kXchg + quad]);
+      if (!warp_wait(&bars[kXchg + quad], xc & 1)) return false;
+      other = slot[(1 - hf) * kRows + r];
+      ++xc;
+      return true;
+    };
+    Item it;
+    for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
+      if (it.n == 0) continue;
+      const int* table = p.block_table + (long long)it.b * p.table_stride;
+      const bool valid_row = r < p.rows_used && rq < it.qx;
+      const int limit = valid_row ? it.prefix + it.q0 + rq : it.key_end - 1;  // last visible key
+      float m_used = -INFINITY, l = 0.0f;  // running max the probabilities are scaled by
+      for (int j = 0; j < it.n; ++j, ++t) {
+        const int buf = t % kSBufs;
+        const int key0 = j * kKeys;
+        const bool ok = page_ok(table[key0 / p.block_size], p.num_blocks);
+        if (!warp_wait(&bars[kSFull + buf], (t / kSBufs) & 1)) {
           alive = false;
           break;
         }
         tc_fence_after();
-        float s[kKeys];
+        const uint32_t scol = lane_base + buf * kKeys;
+        float s[64];
         {
-          uint32_t raw0[32], raw1[32];
-          tmem_ld32(trow + sb * kKeys, raw0);
-          tmem_ld32(trow + sb * kKeys + 32, raw1);
+          uint32_t a0[32], a1[32];
+          tmem_ld32(scol + hf * 64, a0);
+          tmem_ld32(scol + hf * 64 + 32, a1);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            s[i] = __uint_as_float(raw0[i]);
-            s[32 + i] = __uint_as_float(raw1[i]);
+          for (int c = 0; c < 32; ++c) {
+            s[c] = __uint_as_float(a0[c]);
+            s[32 + c] = __uint_as_float(a1[c]);
           }
         }
-        if (j >= it.full_tiles || !ok) {
-          const int lim = ok ? min(limit, it.kv_len - 1) - key0 : -1;
+        if (j >= it.full || !ok) {
+          const int lim = (ok ? min(limit, it.kv_len - 1) - key0 : -1) - hf * 64;
 #pragma unroll
-          for (int c = 0; c < kKeys; ++c)
+          for (int c = 0; c < 64; ++c)
             if (c > lim) s[c] = -INFINITY;
         }
         float mx8[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = s[i];
+        for (int i8 = 0; i8 < 8; ++i8) mx8[i8] = s[i8];
 #pragma unroll
-        for (int c = 8; c < kKeys; c += 16) {
+        for (int c = 8; c < 56; c += 16) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) mx8[i] = max3(mx8[i], s[c + i], s[c + 8 + i]);
+          for (int i8 = 0; i8 < 8; ++i8) mx8[i8] = max3(mx8[i8], s[c + i8], s[c + 8 + i8]);
         }
-        const float mx = max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
-        const float m_tile = mx * sl2;
+#pragma unroll
+        for (int i8 = 0; i8 < 8; ++i8) mx8[i8] = fmaxf(mx8[i8], s[56 + i8]);
+        const float pm = max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+        // The other half may overwrite S columns this half has read (its P
+        // store) once both have arrived.
+        tc_fence_before();
+        float om;
+        if (!exchange(pm, om)) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        const float m_tile = fmaxf(pm, om) * sl2;
         // Rescale only when the row max grew by more than 2^8 (or on the
-        // first finite max); otherwise keep scaling by the stale max.
+        // first finite max); otherwise keep scaling by the stale max. Both
+        // halves see the same values, so they decide alike.
         float alpha = 1.0f;
         if (m_tile > m_used + kRescaleLog2) {
           alpha = fast_exp2(m_used - m_tile);  // 0 when m_used = -inf
@@ -501,9 +660,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float nm = m_used == -INFINITY ? 0.0f : -m_used;
         float sum[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sum[i] = 0.0f;
+        for (int i8 = 0; i8 < 8; ++i8) sum[i8] = 0.0f;
+        uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < kKeys; c += 2) {
+        for (int c = 0; c < 64; c += 2) {
           fma2(s[c], s[c + 1], s[c], s[c + 1], sl2, sl2, nm, nm);
           if ((c & 15) == 14) {
             exp2_fma_pair(s[c], s[c + 1]);  // one pair in eight on the FMA pipe
@@ -513,61 +673,34 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
           const int k = (c >> 1) & 3;  // four independent accumulator pairs
           add2(sum[2 * k], sum[2 * k + 1], sum[2 * k], sum[2 * k + 1], s[c], s[c + 1]);
+          pk[c >> 1] = pack_bf16x2(s[c], s[c + 1]);
         }
+        // keys [64 hf, +64) -> packed columns [32 hf, +32) of this buffer
+        tmem_st32(scol + hf * 32, pk);
         l = l * alpha + (((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7])));
-
-        // P_g as packed BF16 pairs over the first 32 columns of S_g.
-        {
-          uint32_t pk[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(s[2 * i], s[2 * i + 1]);
-          tmem_st32(trow + sb * kKeys, pk);
-        }
-        // One o_done phase per tile (PV_{g-1}); the item's first tile needs
-        // none: the previous epilogue consumed that phase.
-        if (j >= 1) {
-          if (!mbar_wait(&bars[kODone], (g - 1) & 1, kErrPrefillWait)) {
+        // O is quiescent once PV_{t-1} has completed (PV_t waits for this P).
+        if (t >= 1) {
+          const int pb = (t - 1) % kSBufs;
+          if (!warp_wait(&bars[kPVDone + pb], ((t - 1) / kSBufs) & 1)) {
             alive = false;
             break;
           }
           tc_fence_after();
         }
-        // V rows that are not real keys (past kv_len, or an invalid page) are
-        // zeroed so that P = 0 never meets a non-finite cache value. All PVs
-        // before g are complete here, so this vfull wait is for V_g itself.
-        const int real_keys = ok ? min(kKeys, it.kv_len - key0) : 0;
-        if (real_keys < kKeys) {
-          const int st = g % kStages;
-          if (!mbar_wait(&bars[kVFull + st], (g / kStages) & 1, kErrPrefillWait)) {
-            alive = false;
-            break;
-          }
-          if (r < kKeys && r >= real_keys) {
-            const uint32_t vrow = sbase + kVOff + st * kKVBytes + r * 128;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              st_shared_zero16(vrow + c * 16);
-              st_shared_zero16(vrow + kKVHalf + c * 16);
-            }
-          }
-          fence_proxy_async_smem();
-        }
         if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+          // this half rescales O columns [64 hf, +64)
+          uint32_t o0[32], o1[32];
+          const uint32_t oaddr = lane_base + kOCol + hf * 64;
+          tmem_ld32(oaddr, o0);
+          tmem_ld32(oaddr + 32, o1);
+          tmem_ld_wait();
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t o0[32], o1[32];
-            const uint32_t oaddr = trow + kOCol + half * 64;
-            tmem_ld32(oaddr, o0);
-            tmem_ld32(oaddr + 32, o1);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              o0[i] = __float_as_uint(__uint_as_float(o0[i]) * alpha);
-              o1[i] = __float_as_uint(__uint_as_float(o1[i]) * alpha);
-            }
-            tmem_st32(oaddr, o0);
-            tmem_st32(oaddr + 32, o1);
+          for (int c = 0; c < 32; ++c) {
+            o0[c] = __float_as_uint(__uint_as_float(o0[c]) * alpha);
+            o1[c] = __float_as_uint(__uint_as_float(o1[c]) * alpha);
           }
+          tmem_st32(oaddr, o0);
+          tmem_st32(oaddr + 32, o1);
         }
         tmem_st_wait();
         tc_fence_before();
@@ -575,18 +708,53 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (lane == 0) mbar_arrive(&bars[kPFull]);
       }
       if (!alive) break;
-
-      // epilogue: O / l -> BF16 rows of `out`, natural-log LSE; then O is free
-      const int g_last = gt + it.n_tiles - 1;
-      if (!mbar_wait(&bars[kODone], g_last & 1, kErrPrefillWait)) break;
+      // Row sum = both halves' sums; half 0 hands (max used, sum) to the
+      // epilogue (one slot, freed by it).
+      float lo;
+      if (!exchange(l, lo)) break;
+      if (hf == 0) {
+        if (ix > 0 && !warp_wait(&bars[kStatsFree], (ix - 1) & 1)) break;
+        // no finite score seen: the sum holds only clamped-exponent residue
+        stats[r] = make_float2(m_used, m_used == -INFINITY ? 0.0f : l + lo);
+        mbar_arrive(&bars[kStatsFull]);
+      }
+      ++ix;
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
+    const int rq = r / p.group;
+    int ix = 0;
+    bool alive = true;
+    Item it;
+    for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
+      const int qpos = it.q0 + rq;
+      const bool valid_row = r < p.rows_used && rq < it.qx && qpos < p.max_q;
+      const int head = it.h * p.group + (r % p.group);
+      __nv_bfloat16* dst = p.out + (((long long)it.q_begin + qpos) * p.qh + head) * 128;
+      float* lse_dst = p.lse ? p.lse + ((long long)it.b * p.qh + head) * p.max_q + qpos : nullptr;
+      if (it.n == 0) {
+        // No visible keys (invalid context): zero rows, -inf LSE.
+        if (valid_row) {
+          for (int d = 0; d < 128; d += 8) *reinterpret_cast<uint4*>(dst + d) = make_uint4(0, 0, 0, 0);
+          if (lse_dst) *lse_dst = -INFINITY;
+        }
+        continue;
+      }
+      if (!warp_wait(&bars[kStatsFull], ix & 1)) break;
+      const float2 ml = stats[r];
+      mbar_arrive(&bars[kStatsFree]);
+      if (!warp_wait(&bars[kODone], ix & 1)) break;
       tc_fence_after();
+      const float l = ml.y;
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-      __nv_bfloat16* dst = p.out + (tok * p.qh + head) * 128;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      for (int h = 0; h < 2; ++h) {
         uint32_t o0[32], o1[32];
-        tmem_ld32(trow + kOCol + half * 64, o0);
-        tmem_ld32(trow + kOCol + half * 64 + 32, o1);
+        tmem_ld32(lane_base + kOCol + h * 64, o0);
+        tmem_ld32(lane_base + kOCol + h * 64 + 32, o1);
         tmem_ld_wait();
         if (valid_row) {
 #pragma unroll
@@ -597,19 +765,18 @@ __global__ void __launch_bounds__(kThreads, 2)
             w.y = pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
             w.z = pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
             w.w = pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
-            *reinterpret_cast<uint4*>(dst + half * 64 + vv * 8) = w;
+            *reinterpret_cast<uint4*>(dst + h * 64 + vv * 8) = w;
           }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kOFree]);
-      if (valid_row && p.lse) {
-        const float m_out = m_used == -INFINITY ? 0.0f : m_used;
-        p.lse[((long long)it.b * p.qh + head) * p.max_q + it.q0 + rq] =
-            l > 0.0f ? (m_out + fast_log2(l)) * kLn2 : -INFINITY;
+      if (valid_row && lse_dst) {
+        const float m_out = ml.x == -INFINITY ? 0.0f : ml.x;
+        *lse_dst = l > 0.0f ? (m_out + fast_log2(l)) * kLn2 : -INFINITY;
       }
-      gt += it.n_tiles;
+      ++ix;
     }
   }
 
@@ -619,6 +786,47 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
+  if (threadIdx.x == 0) {
+    // The last CTA to finish resets the claim counter for the next launch on
+    // this stream (every CTA's claims precede its increment here).
+    __threadfence();
+    if (atomicAdd(p.sched + 1, 1) == int(gridDim.x) - 1) {
+      atomicExch(p.sched, 0);
+      atomicExch(p.sched + 1, 0);
+    }
+  }
+}
+
+// Claim counters {next item, CTAs finished}, one pair per stream that
+// launches the prefill (a launch leaves its pair at zero when it ends).
+__device__ int g_prefill_sched[64][2];
+
+// Pair for (stream, device): streams get their own pair in order of first
+// use; past 64 streams pairs are shared by hash, and launches sharing a pair
+// must not overlap in time.
+int* sched_pair(cudaStream_t stream, int dev, cudaError_t* err) {
+  static std::mutex mu;
+  static int* base[64] = {};
+  static cudaStream_t keys_s[64];
+  static int keys_d[64];
+  static int used = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!base[dev & 63]) {
+    void* ptr = nullptr;
+    *err = cudaGetSymbolAddress(&ptr, g_prefill_sched);
+    if (*err != cudaSuccess) return nullptr;
+    base[dev & 63] = static_cast<int*>(ptr);
+  }
+  int slot = -1;
+  for (int i = 0; i < used; ++i)
+    if (keys_s[i] == stream && keys_d[i] == dev) slot = i;
+  if (slot < 0 && used < 64) {
+    keys_s[used] = stream;
+    keys_d[used] = dev;
+    slot = used++;
+  }
+  if (slot < 0) slot = int((reinterpret_cast<uintptr_t>(stream) >> 4) & 63);
+  return base[dev & 63] + 2 * slot;
 }
 
 }  // namespace prefill_detail
@@ -668,9 +876,6 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   if (!(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit)) {
     e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return e;
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
   static int sm_count[64] = {};
@@ -680,10 +885,12 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     sm_count[dev & 63] = n;
   }
+  p.sched = sched_pair(stream, dev, &e);
+  if (!p.sched) return e;
   p.n_qtiles = (a.max_q + qt - 1) / qt;
   const long long items = (long long)p.n_qtiles * a.batch * a.kvh;
   if (items > 0x7fffffffLL) return cudaErrorNotSupported;
-  const int grid = int(items < 2LL * sm_count[dev & 63] ? items : 2LL * sm_count[dev & 63]);
+  const int grid = int(items < sm_count[dev & 63] ? items : sm_count[dev & 63]);
   prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p, *qmap, *kmap, *vmap);
   return cudaGetLastError();
 }

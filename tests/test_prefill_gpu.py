@@ -84,3 +84,38 @@ def test_single_query_rows_mixed_with_long_groups(nvb, oracle):
     W = nvb.workloads
     case = W.paged_case([1, 513, 2, 700], [1, 300, 2, 1], q_heads=16, kv_heads=8, seed=21, scale=1.0)
     _check(nvb, oracle, case, what="mixed q lens")
+
+
+@pytest.mark.parametrize("qh,kvh", [(128, 8), (24, 8)])
+def test_prefill_group_16_and_partial_rows(nvb, oracle, qh, kvh):
+    # 16 heads per kv head (8 queries per 128-row sub-tile) and 3 heads per
+    # kv head (126 of 128 rows used)
+    W = nvb.workloads
+    case = W.paged_case([77, 400, 1030], [77, 150, 300], q_heads=qh, kv_heads=kvh, seed=qh + 1, scale=1.0)
+    _check(nvb, oracle, case, what=f"{qh}q/{kvh}kv")
+
+
+def test_prefill_nan_past_kv_len_and_invalid_page(nvb, oracle):
+    # Cache rows past each sequence's length hold NaN (they must meet only
+    # P = 0 and be zeroed first); page 1 of sequence 1 is invalid (-1), so
+    # keys 256..511 of that sequence are masked, as in the oracle.
+    W = nvb.workloads
+    case = W.paged_case([300, 700, 130], [300, 200, 130], q_heads=16, kv_heads=8, seed=5, scale=1.0)
+    bs = case.block_size
+    for b, n in enumerate(case.kv_lens.tolist()):
+        page = int(case.block_table[b, (n - 1) // bs])
+        if n % bs:
+            case.k[page, n % bs:] = float("nan")
+            case.v[page, n % bs:] = float("nan")
+    case.block_table[1, 1] = -1
+    out, _ = _run(nvb, case)
+    assert torch.isfinite(out.float()).all()
+    _check(nvb, oracle, case, what="nan tail / invalid page")
+
+
+def test_prefill_more_items_than_sms(nvb, oracle):
+    # 2500 + 1800 queries x 8 kv heads: more work items than SMs, so CTAs of
+    # the persistent kernel run several items and reuse Q / O buffers.
+    W = nvb.workloads
+    case = W.paged_case([2500, 1800], [2500, 1800], q_heads=16, kv_heads=8, seed=11, scale=1.0)
+    _check(nvb, oracle, case, what="persistent items")
