@@ -14,7 +14,9 @@ Multi-GPU runs are weak-scaled: each rank decodes its own 256-sequence shard
            the step's inputs (new-token QKV projections, positions, slots,
            page tables, kv_lens) go H2D from pinned memory, the fused
            norm/RoPE/KV-store kernel writes the new token into the cache,
-           decode attention runs, and the output comes back D2H.
+           decode attention runs, and the output comes back D2H. The step
+           is pipelined over sequence chunks (--e2e-chunks) so that one
+           chunk's copies overlap another's kernels.
   prefill  varlen causal prefill TFLOP/s on BASELINE config 2 (32 prompts,
            lengths U[64, 2048], 16q/8kv), causal FLOPs of visible keys only.
 
@@ -263,6 +265,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunks", type=int, default=2,
+                    help="sequence chunks the end-to-end step is pipelined over (copies overlap compute)")
     ap.add_argument("--no-long-context", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 256 = config 3; smaller only for profiler captures)")
@@ -364,27 +368,74 @@ def main():
         h2d = sum(t.numel() * t.element_size() for t in host_in.values())
         d2h = out_h.numel() * out_h.element_size()
 
+        # The step is pipelined over sequence chunks on three streams: chunk
+        # c+1's inputs go H2D while chunk c runs the fused store and decode,
+        # and chunk c's output goes D2H while chunk c+1 runs. Every input and
+        # output byte of the step still crosses PCIe inside the timed region.
+        # Step k+1's uploads wait for step k's compute (the next token's
+        # projections depend on this step), and its compute waits for step
+        # k's downloads (the output buffer is reused).
+        nch = max(1, min(args.e2e_chunks, batch))
+        bounds = [(c * batch // nch, (c + 1) * batch // nch) for c in range(nch)]
+        h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        chunk_cfg = []
+        for s0, s1 in bounds:
+            n = s1 - s0
+            sp = nvb.num_splits(n, QH, KVH, CTX, sms)
+            la_c, oa_c = nvb.splitkv_scratch(sp, n, QH, dev) if sp > 1 else (None, None)
+            chunk_cfg.append((s0, s1, sp, la_c, oa_c))
+        ev_in = [torch.cuda.Event() for _ in bounds]
+        ev_done = [torch.cuda.Event() for _ in bounds]
+
         def e2e_step():
-            for n, t in host_in.items():
-                dev_in[n].copy_(t, non_blocking=True)
-            nvb.qkv_rope_cached(dev_in["qkv"], qw, kw, dev_in["pos"], dev_in["slots"], q_dev, case.k, case.v, rows=batch,
-                                q_heads=QH, kv_heads=KVH, head_dim=DIM, block_size=BS, num_blocks=case.num_blocks,
-                                eps=1e-6, rope_cache=rope, max_positions=CTX)
-            nvb.paged_fwd(q_dev, case.k, case.v, out, dev_in["cuq"], dev_in["lens"], dev_in["table"], batch=batch,
-                          max_q=1, max_k=CTX, q_heads=QH, kv_heads=KVH, block_size=BS, table_stride=case.table_stride,
-                          num_blocks=case.num_blocks, num_splits=splits, lse=lse, lse_accum=la, out_accum=oa)
-            out_h.copy_(out, non_blocking=True)
+            h2d_s.wait_stream(stream)
+            with torch.cuda.stream(h2d_s):
+                for n_, t in host_in.items():
+                    if n_ != "qkv":
+                        dev_in[n_].copy_(t, non_blocking=True)
+                for c, (s0, s1, *_r) in enumerate(chunk_cfg):
+                    dev_in["qkv"][s0:s1].copy_(qkv_h[s0:s1], non_blocking=True)
+                    ev_in[c].record(h2d_s)
+            stream.wait_stream(d2h_s)
+            for c, (s0, s1, sp, la_c, oa_c) in enumerate(chunk_cfg):
+                n = s1 - s0
+                stream.wait_event(ev_in[c])
+                nvb.qkv_rope_cached(dev_in["qkv"][s0:s1], qw, kw, dev_in["pos"][s0:s1], dev_in["slots"][s0:s1],
+                                    q_dev[s0:s1], case.k, case.v, rows=n, q_heads=QH, kv_heads=KVH, head_dim=DIM,
+                                    block_size=BS, num_blocks=case.num_blocks, eps=1e-6, rope_cache=rope,
+                                    max_positions=CTX)
+                nvb.paged_fwd(q_dev[s0:s1], case.k, case.v, out[s0:s1], dev_in["cuq"][:n + 1], dev_in["lens"][s0:s1],
+                              dev_in["table"][s0:s1], batch=n, max_q=1, max_k=CTX, q_heads=QH, kv_heads=KVH,
+                              block_size=BS, table_stride=case.table_stride, num_blocks=case.num_blocks,
+                              num_splits=sp, lse=lse[s0:s1], lse_accum=la_c, out_accum=oa_c)
+                ev_done[c].record(stream)
+            with torch.cuda.stream(d2h_s):
+                for c, (s0, s1, *_r) in enumerate(chunk_cfg):
+                    d2h_s.wait_event(ev_done[c])
+                    out_h[s0:s1].copy_(out[s0:s1], non_blocking=True)
 
         e2e_steps = max(10, min(args.steps, 200))
         for _ in range(3):
             e2e_step()
+        stream.wait_stream(d2h_s)
         torch.cuda.synchronize()
+        # the pipelined step must give the whole-batch result (not timed)
+        ref_out = torch.empty_like(out)
+        nvb.paged_fwd(q_dev, case.k, case.v, ref_out, dev_in["cuq"], dev_in["lens"], dev_in["table"], batch=batch,
+                      max_q=1, max_k=CTX, q_heads=QH, kv_heads=KVH, block_size=BS, table_stride=case.table_stride,
+                      num_blocks=case.num_blocks, num_splits=splits, lse=lse, lse_accum=la, out_accum=oa)
+        torch.cuda.synchronize()
+        e2e_err = (out_h.float() - ref_out.cpu().float()).abs().max().item()
+        if not e2e_err <= 2e-2:
+            raise RuntimeError(f"pipelined end-to-end step differs from the whole-batch decode: max-abs {e2e_err}")
+        del ref_out
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(e2e_steps):
             e2e_step()
+        stream.wait_stream(d2h_s)
         e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms = e0.elapsed_time(e1)
@@ -467,8 +518,9 @@ def main():
             "long_context": long_ctx,
             "e2e": None if e2e_value is None else {
                 "value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(e2e_ms / e2e_steps, 5),
-                "path": "pinned H2D of step inputs -> nvb_qkv_rope_cached -> nvb_paged_fwd_ex -> D2H output"},
+                "ms_per_step": round(e2e_ms / e2e_steps, 5), "chunks": nch,
+                "path": "per sequence chunk: pinned H2D of step inputs -> nvb_qkv_rope_cached -> nvb_paged_fwd_ex -> "
+                        "D2H output, chunks pipelined on H2D / compute / D2H streams"},
             "gpu_launches": args.steps * (1 if splits == 1 else 2),
             "gpu_launches_note": "decode_mma_kernel launches (+ combine_kernel when num_splits > 1) in the timed region",
             "clocks": clock_rec,
