@@ -96,8 +96,8 @@ int nvb_paged_decode_static_scratch(void* stream, const void* q, const void* k, 
 
 /* Split count for decode, replacing `nvr_flash_num_splits`
  * (kernels/flash_native/flash_native.h:31-32, flash_native.cu:17-38).
- * A B200 heuristic: enough (sequence, kv head, split) CTAs to fill
- * 2 CTAs per SM for a few waves, with at least 256 KV tokens per split.
+ * A B200 heuristic: the most (sequence, kv head, split) CTAs that fit one
+ * wave of 2 CTAs per SM, with at least 256 KV tokens per split.
  * Pass the physical SM count. Invalid arguments return 0. */
 int nvb_num_splits(int batch, int q_heads, int kv_heads, int max_k, int num_sms);
 

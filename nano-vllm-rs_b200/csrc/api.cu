@@ -307,7 +307,11 @@ int nvb_num_splits(int batch, int q_heads, int kv_heads, int max_k, int num_sms)
   const long long work = (long long)batch * kv_heads * (group / gc);
   const long long target = 2LL * num_sms;  // two resident CTAs per SM
   if (work >= target) return 1;
-  long long splits = (target + work - 1) / work;
+  // The most splits that still fit one wave of resident CTAs: a split count
+  // one past it leaves a sparse second wave too small to keep HBM busy
+  // (4 x 8 heads x 10 splits = 320 CTAs on 296 slots ran at 0.62 of copy
+  // bandwidth).
+  long long splits = target / work;
   const long long max_by_len = (max_k + 255) / 256;  // keep >= 256 keys per split
   if (splits > max_by_len) splits = max_by_len;
   if (splits > 128) splits = 128;

@@ -39,7 +39,8 @@ def test_num_splits_heuristic(nvb):
     assert nvb.num_splits(0, 16, 8, 4096, 148) == 0
     assert nvb.num_splits(4, 16, 5, 4096, 148) == 0
     assert nvb.num_splits(256, 32, 8, 4096, 148) == 1          # 2048 CTAs already fill the GPU
-    assert nvb.num_splits(8, 16, 8, 4096, 148) == 5            # 64 CTAs -> 5 splits (296 target)
+    assert nvb.num_splits(8, 16, 8, 4096, 148) == 4            # 64 CTAs x 4 = 256 fit one wave of 296
+    assert nvb.num_splits(4, 64, 8, 32768, 148) == 9           # config 5 on one GPU: 288 CTAs, not 320
     assert nvb.num_splits(4, 8, 1, 32768, 148) == 74           # config 5 shard
     assert nvb.num_splits(1, 16, 8, 300, 148) == 2             # >= 256 keys per split
     assert 1 <= nvb.num_splits(1, 256, 1, 1 << 20, 148) <= 128
