@@ -213,9 +213,10 @@ def run_reference(args, rank, world):
 def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
     """Qwen3-32B attention shape (64q/8kv), 4 sequences of
     ctx 32768. At N GPUs each rank owns 8/N kv heads (and their query heads),
-    runs split-KV decode on its shard and all-gathers the BF16 outputs over
-    NCCL. Returns whole-job GB/s of algorithmic bytes, timed with CUDA events
-    (max over ranks)."""
+    runs split-KV decode on its shard, and the combine kernel stores every
+    result into all ranks' outputs over NVLink (nvb_paged_decode_gather: one
+    launch pair per step, no NCCL). Returns whole-job GB/s of algorithmic
+    bytes, timed with CUDA events (max over ranks)."""
     import importlib
 
     import torch
@@ -226,7 +227,7 @@ def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
     shard = S.HeadShard(rank, world, kv_heads=kvh, q_heads=qh)
     case = W.paged_case([ctx] * batch, q_heads=shard.q_local, kv_heads=shard.kv_local, seed=500 + rank, device=dev)
     run = S.KvHeadShardedDecode(nvb, shard, batch=batch, block_size=256, table_stride=case.table_stride,
-                                num_blocks=case.num_blocks, max_k=ctx, device=dev)
+                                num_blocks=case.num_blocks, max_k=ctx, device=dev, fused=world > 1)
 
     def once():
         if world > 1:
@@ -249,10 +250,15 @@ def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = t.item()
+    err = nvb.device_error()
+    run.close()  # every rank's GPU work is done (the all-reduce above)
+    if err:
+        raise RuntimeError(f"long-context decode recorded device error {err}")
     total_bytes = batch * ctx * kvh * 512 + 2 * batch * qh * 128 * 2
     return {"value": round(total_bytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 5),
             "splits_per_gpu": run.splits, "kv_heads_per_gpu": shard.kv_local,
-            "collective": "NCCL all-gather of BF16 outputs" if world > 1 else None,
+            "collective": ("combine fused with the all-gather: peer stores over NVLink + epoch-flag barrier "
+                           "(nvb_paged_decode_gather)") if world > 1 else None,
             "workload": "config5: 4 seqs x ctx 32768, 64q/8kv, kv-head sharded over the GPUs, split-KV per GPU"}
 
 

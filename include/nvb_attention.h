@@ -101,6 +101,40 @@ int nvb_paged_decode_static_scratch(void* stream, const void* q, const void* k, 
  * Pass the physical SM count. Invalid arguments return 0. */
 int nvb_num_splits(int batch, int q_heads, int kv_heads, int max_k, int num_sms);
 
+/* Multi-GPU decode over kv-head shards (no counterpart in the reference,
+ * which is single-GPU). One process per GPU of a node; rank r holds kv
+ * heads [r*kv_heads, (r+1)*kv_heads) of the cache and passes its q
+ * [batch, q_heads, 128] (the query heads of those kv heads). The split-KV
+ * combine stores each result into every rank's output
+ * [batch, world*q_heads, 128] at head offset r*q_heads (peer stores over
+ * NVLink), then a one-warp barrier exchanges `epoch` with every rank; when
+ * the call's work on `stream` is done, every rank's contributions are in this
+ * rank's output. Arguments as nvb_paged_fwd_ex (max_q = 1, no lse) plus:
+ *   out_local   [batch, q_heads, 128] BF16 scratch (used when num_splits == 1)
+ *   peer_out    host array of `world` device pointers: each rank's output
+ *   peer_flag   host array of `world` device pointers: each rank's flags,
+ *               at least `world` uint32 starting at 0 (one slot per rank)
+ *   epoch       strictly increasing per call (1, 2, ...), the same on every rank
+ * Every rank must make the call with the same epoch; a rank that does not
+ * leaves the others' barrier to give up after about two seconds, recording
+ * device error 7 (nvb_device_error). Output buffers are written by all
+ * ranks: alternate two of them between steps, so that no rank writes a
+ * buffer another rank may still be reading. */
+int nvb_paged_decode_gather(void* stream, const void* q, const void* k, const void* v, void* out_local,
+                            const int* cu_q, const int* kv_lens, const int* block_table, int batch, int max_k,
+                            int q_heads, int kv_heads, int block_size, int table_stride, int num_blocks,
+                            int num_splits, float* lse_accum, float* out_accum, void* const* peer_out,
+                            unsigned int* const* peer_flag, int world, int rank, unsigned int epoch);
+
+/* Device buffers shared between the ranks of a node through CUDA IPC (the
+ * outputs and flags of nvb_paged_decode_gather). create: cudaMalloc `bytes`
+ * (zeroed) and write its 64-byte IPC handle; open: map a peer's handle;
+ * close: unmap a peer's mapping; free: release this rank's buffer. */
+int nvb_peer_buffer_create(size_t bytes, void** ptr, void* ipc_handle);
+int nvb_peer_buffer_open(const void* ipc_handle, void** ptr);
+int nvb_peer_buffer_close(void* ptr);
+int nvb_peer_buffer_free(void* ptr);
+
 /* Thread-local message for the last failing call on this thread
  * (kernels/flash_native/flash_native.cu:15, kernels/kernels.cu:28). */
 const char* nvb_last_error(void);

@@ -47,6 +47,11 @@ def _declare(lib):
         "nvb_graph_destroy": [_P],
         "nvb_device_error": [ctypes.POINTER(c_int)],
         "nvb_clear_device_error": [],
+        "nvb_paged_decode_gather": [_P] * 8 + [c_int] * 8 + [_P] * 4 + [c_int, c_int, ctypes.c_uint],
+        "nvb_peer_buffer_create": [ctypes.c_size_t, ctypes.POINTER(c_void_p), _P],
+        "nvb_peer_buffer_open": [_P, ctypes.POINTER(c_void_p)],
+        "nvb_peer_buffer_close": [_P],
+        "nvb_peer_buffer_free": [_P],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)
@@ -134,6 +139,61 @@ def splitkv_scratch(num_splits_, batch, q_heads, device):
     lse_accum = torch.empty(num_splits_, batch, q_heads, dtype=torch.float32, device=device)
     out_accum = torch.empty(num_splits_, batch, q_heads, 128, dtype=torch.float32, device=device)
     return lse_accum, out_accum
+
+
+def peer_buffer_create(nbytes):
+    """A zeroed device buffer of this GPU to share with the node's other ranks:
+    returns (device pointer, 64-byte CUDA IPC handle)."""
+    ptr = c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    _check(library().nvb_peer_buffer_create(nbytes, ctypes.byref(ptr), handle))
+    return ptr.value, handle.raw
+
+
+def peer_buffer_open(handle):
+    """Maps another rank's buffer (its IPC handle) into this process."""
+    ptr = c_void_p()
+    buf = ctypes.create_string_buffer(bytes(handle), 64)
+    _check(library().nvb_peer_buffer_open(buf, ctypes.byref(ptr)))
+    return ptr.value
+
+
+def peer_buffer_close(ptr):
+    _check(library().nvb_peer_buffer_close(c_void_p(ptr)))
+
+
+def peer_buffer_free(ptr):
+    _check(library().nvb_peer_buffer_free(c_void_p(ptr)))
+
+
+def paged_decode_gather(q, k, v, out_local, cu_q, kv_lens, block_table, *, batch, max_k, q_heads, kv_heads,
+                        block_size, table_stride, num_blocks, num_splits, lse_accum, out_accum, peer_out, peer_flag,
+                        rank, epoch, stream=None, check=True):
+    """Decode of this rank's kv heads with the combine fused into the
+    all-gather of the outputs (nvb_paged_decode_gather): `peer_out` and
+    `peer_flag` are every rank's output and flag device pointers (ints)."""
+    import torch
+
+    world = len(peer_out)
+    if check:
+        _tensor(q, (batch, q_heads, 128), torch.bfloat16, "q")
+        _tensor(out_local, (batch, q_heads, 128), torch.bfloat16, "out_local")
+        for t, nm in ((k, "k"), (v, "v")):
+            _tensor(t, (num_blocks, block_size, kv_heads, 128), torch.bfloat16, nm)
+        _tensor(cu_q, (batch + 1,), torch.int32, "cu_q")
+        _tensor(kv_lens, (batch,), torch.int32, "kv_lens")
+        _tensor(block_table, (batch, table_stride), torch.int32, "block_table")
+        if num_splits > 1:
+            _tensor(lse_accum, (num_splits, batch, q_heads), torch.float32, "lse_accum")
+            _tensor(out_accum, (num_splits, batch, q_heads, 128), torch.float32, "out_accum")
+        if len(peer_flag) != world or not 1 <= world <= 8:
+            raise ValueError("peer_out and peer_flag need one pointer per rank (1..8 ranks)")
+    outs = (c_void_p * world)(*peer_out)
+    flags = (c_void_p * world)(*peer_flag)
+    _check(library().nvb_paged_decode_gather(
+        _stream(stream), _ptr(q), _ptr(k), _ptr(v), _ptr(out_local), _ptr(cu_q), _ptr(kv_lens), _ptr(block_table),
+        batch, max_k, q_heads, kv_heads, block_size, table_stride, num_blocks, num_splits, _ptr(lse_accum),
+        _ptr(out_accum), ctypes.cast(outs, c_void_p), ctypes.cast(flags, c_void_p), world, rank, epoch))
 
 
 def paged_fwd(q, k, v, out, cu_q, kv_lens, block_table, *, batch, max_q, max_k, q_heads, kv_heads,

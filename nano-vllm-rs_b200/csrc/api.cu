@@ -133,7 +133,10 @@ int kv_mma_map(const void* cache, long long tokens, int kvh, const CUtensorMap**
   return make_map_3d(cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, out);
 }
 
-int run_decode(cudaStream_t stream, DecodeParams p, const void* k, const void* v) {
+// `combine` false leaves split-KV partials in lse_accum / out_accum for the
+// caller's own combine (the multi-GPU gather path); only the tensor-core
+// decode can stop there.
+int run_decode(cudaStream_t stream, DecodeParams p, const void* k, const void* v, bool combine = true) {
   const long long tokens = (long long)p.num_blocks * p.block_size;
   const CUtensorMap* kmap = nullptr;
   const CUtensorMap* vmap = nullptr;
@@ -144,11 +147,12 @@ int run_decode(cudaStream_t stream, DecodeParams p, const void* k, const void* v
     p.n_hgroups = 1;
     cudaError_t e = launch_decode_mma(p, *kmap, *vmap, stream);
     if (e != cudaErrorNotSupported) {
-      if (e == cudaSuccess && p.num_splits > 1) e = launch_combine(p, stream);
+      if (e == cudaSuccess && p.num_splits > 1 && combine) e = launch_combine(p, stream);
       return cuda_status(e, "decode attention launch");
     }
     cudaGetLastError();
   }
+  if (!combine) return fail("split partials need the tensor-core decode (block_size a multiple of 128)");
   if (int rc = kv_decode_map(k, tokens, p.kvh, &kmap)) return rc;
   if (int rc = kv_decode_map(v, tokens, p.kvh, &vmap)) return rc;
   p.scale_log2 = kScaleLog2;
@@ -158,7 +162,7 @@ int run_decode(cudaStream_t stream, DecodeParams p, const void* k, const void* v
 int paged_fwd_impl(void* stream, const void* q, const void* k, const void* v, void* out, const int* cu_q,
                    const int* kv_lens, const int* block_table, int batch, int total_q, int max_q, int max_k,
                    int q_heads, int kv_heads, int block_size, int table_stride, int num_splits, float* lse,
-                   float* lse_accum, float* out_accum, int num_blocks, bool bounded) {
+                   float* lse_accum, float* out_accum, int num_blocks, bool bounded, bool combine = true) {
   g_last_error[0] = 0;
   // Same checks as kernels/flash_native/flash_native.cu:48-58, except the
   // 4096-token context cap, which this implementation does not have.
@@ -225,7 +229,7 @@ int paged_fwd_impl(void* stream, const void* q, const void* k, const void* v, vo
   p.num_splits = num_splits;
   p.max_q = 1;
   p.mode = kModeDecode;
-  return run_decode(s, p, k, v);
+  return run_decode(s, p, k, v, combine);
 }
 
 int native_impl(void* stream, const void* q, const void* kc, const void* vc, const int* positions,

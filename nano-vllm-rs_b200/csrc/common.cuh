@@ -29,6 +29,7 @@ enum DeviceError : int {
   kErrPrefillTmem = 4,        // TMEM allocation returned an unusable address
   kErrBadPage = 5,            // reserved: a page id outside [0, num_blocks)
   kErrPrefillAlign = 6,       // prefill: dynamic shared memory base not usable for the tile layout
+  kErrGatherWait = 7,         // multi-GPU gather: a peer's completion flag did not arrive in time
 };
 
 constexpr long long kWaitCycles = 4000000000LL;

@@ -1,0 +1,183 @@
+// Multi-GPU decode over kv-head shards: the split-KV combine fused with the
+// all-gather of the outputs.
+//
+// Long contexts (4 x 32768 tokens, 64q/8kv) are sharded over the GPUs of a
+// node by kv head: rank r owns kv heads [r * kvh_local, (r + 1) * kvh_local)
+// and the query heads of their groups, so its decode reads only its share of
+// the KV cache. Every rank then needs the whole [batch, q_heads, 128] output.
+// Instead of a separate collective after the decode, the combine kernel below
+// stores each (sequence, head) result straight into every rank's output
+// buffer (peer stores over NVLink through CUDA IPC mappings), and a one-warp
+// barrier kernel exchanges a per-step epoch flag with every peer, so that when
+// a rank's stream moves on, all peers' stores into its buffer have landed.
+//
+// The reference is single-GPU (its README: no NCCL, MPI or tensor
+// parallelism); this path has no counterpart there. No TMA, no multicast and
+// no library kernel touches peer memory: only plain stores and the flags.
+// The barrier's waits are bounded (kWaitCycles) and record kErrGatherWait.
+#include "internal.cuh"
+
+namespace nvb {
+
+namespace gather_detail {
+
+constexpr int kMaxRanks = 8;
+
+struct PeerPtrs {
+  __nv_bfloat16* out[kMaxRanks];  // each rank's output [rows, qh_total, 128] for this step
+  unsigned int* flag[kMaxRanks];  // each rank's flags: slot p = last epoch rank p signalled there
+};
+
+// One warp per (row, local head). splits > 1: weights split s by
+// exp(lse_s - max lse) like combine_kernel (decode.cu); splits == 1: copies
+// the local decode output. The result goes to every rank at head offset
+// head_offset (= rank * qh local).
+__global__ void __launch_bounds__(256) combine_gather_kernel(const float* __restrict__ lse_accum,
+                                                             const float* __restrict__ out_accum,
+                                                             const __nv_bfloat16* __restrict__ local_out, int rows,
+                                                             int qh, int splits, PeerPtrs peers, int world,
+                                                             int head_offset, int qh_total) {
+  const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (item >= (long long)rows * qh) return;
+  uint2 packed;
+  if (splits > 1) {
+    const long long stride = (long long)rows * qh;
+    float mx = -INFINITY;
+    for (int s = lane; s < splits; s += 32) mx = fmaxf(mx, lse_accum[s * stride + item]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float total = 0.0f;
+    if (mx != -INFINITY) {
+      for (int s = 0; s < splits; ++s) {
+        const float ls = lse_accum[s * stride + item];
+        if (ls == -INFINITY) continue;
+        const float w = __expf(ls - mx);
+        total += w;
+        const float4 v = *reinterpret_cast<const float4*>(out_accum + (s * stride + item) * 128 + lane * 4);
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+      }
+    }
+    const float inv = total > 0.0f ? 1.0f / total : 0.0f;
+    packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+    packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+  } else {
+    packed = *reinterpret_cast<const uint2*>(local_out + item * 128 + lane * 4);
+  }
+  const long long row = item / qh, h = item - row * qh;
+  const long long dst = (row * qh_total + head_offset + h) * 128 + lane * 4;
+  for (int p = 0; p < world; ++p) *reinterpret_cast<uint2*>(peers.out[p] + dst) = packed;
+  __threadfence_system();  // the stores are visible to the peers before this thread ends
+}
+
+// One warp: lane p writes this rank's epoch into rank p's flag slot `rank`,
+// then waits until rank p's epoch has arrived in this rank's slot p.
+__global__ void gather_barrier_kernel(PeerPtrs peers, int world, int rank, unsigned int epoch) {
+  const int lane = threadIdx.x;
+  if (lane < world) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.flag[lane] + rank), "r"(epoch) : "memory");
+    const unsigned int* mine = peers.flag[rank] + lane;
+    const long long start = clock64();
+    for (;;) {
+      unsigned int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if (int(v - epoch) >= 0) break;  // epochs only grow (wrap-safe)
+      if (clock64() - start > kWaitCycles) {
+        record_error(kErrGatherWait);
+        break;
+      }
+      __nanosleep(100);
+    }
+  }
+}
+
+}  // namespace gather_detail
+
+}  // namespace nvb
+
+// ------------------------------------------------------------ C ABI
+// Peer buffers: one cudaMalloc'd region per rank, shared with the other ranks
+// of the node through CUDA IPC (no multicast object is created).
+
+extern "C" int nvb_peer_buffer_create(size_t bytes, void** ptr, void* ipc_handle) {
+  using namespace nvb::api_detail;
+  g_last_error[0] = 0;
+  if (!ptr || !ipc_handle || bytes == 0) return fail("invalid peer buffer arguments");
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return cuda_status(e, "cudaMalloc(peer buffer)");
+  e = cudaMemset(*ptr, 0, bytes);  // flags start at epoch 0
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), *ptr);
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return cuda_status(e, "peer buffer set-up");
+  }
+  return 0;
+}
+
+extern "C" int nvb_peer_buffer_open(const void* ipc_handle, void** ptr) {
+  using namespace nvb::api_detail;
+  g_last_error[0] = 0;
+  if (!ptr || !ipc_handle) return fail("invalid peer buffer arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+extern "C" int nvb_peer_buffer_close(void* ptr) {
+  using namespace nvb::api_detail;
+  g_last_error[0] = 0;
+  return cuda_status(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+}
+
+extern "C" int nvb_peer_buffer_free(void* ptr) {
+  using namespace nvb::api_detail;
+  g_last_error[0] = 0;
+  return cuda_status(cudaFree(ptr), "cudaFree(peer buffer)");
+}
+
+extern "C" int nvb_paged_decode_gather(void* stream, const void* q, const void* k, const void* v, void* out_local,
+                                       const int* cu_q, const int* kv_lens, const int* block_table, int batch,
+                                       int max_k, int q_heads, int kv_heads, int block_size, int table_stride,
+                                       int num_blocks, int num_splits, float* lse_accum, float* out_accum,
+                                       void* const* peer_out, unsigned int* const* peer_flag, int world, int rank,
+                                       unsigned int epoch) {
+  using namespace nvb;
+  using namespace nvb::api_detail;
+  using namespace nvb::gather_detail;
+  g_last_error[0] = 0;
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !peer_out || !peer_flag || batch <= 0 ||
+      q_heads <= 0)
+    return fail("invalid gather arguments (world 1..%d, rank in [0, world))", kMaxRanks);
+  PeerPtrs peers{};
+  for (int p = 0; p < world; ++p) {
+    if (!peer_out[p] || !peer_flag[p] || (reinterpret_cast<uintptr_t>(peer_out[p]) & 15) ||
+        (reinterpret_cast<uintptr_t>(peer_flag[p]) & 3))
+      return fail("peer %d: output must be 16-byte aligned and flags 4-byte aligned", p);
+    peers.out[p] = static_cast<__nv_bfloat16*>(peer_out[p]);
+    peers.flag[p] = peer_flag[p];
+  }
+  const bool partials = num_splits > 1 && block_size % 128 == 0;
+  const int rc = paged_fwd_impl(stream, q, k, v, out_local, cu_q, kv_lens, block_table, batch, batch, 1, max_k,
+                                q_heads, kv_heads, block_size, table_stride, num_splits, nullptr, lse_accum,
+                                out_accum, num_blocks, true, !partials);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long items = (long long)batch * q_heads;
+  combine_gather_kernel<<<unsigned((items + 7) / 8), 256, 0, s>>>(
+      lse_accum, out_accum, static_cast<const __nv_bfloat16*>(out_local), batch, q_heads, partials ? num_splits : 1,
+      peers, world, rank * q_heads, world * q_heads);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    gather_barrier_kernel<<<1, 32, 0, s>>>(peers, world, rank, epoch);
+    e = cudaGetLastError();
+  }
+  return cuda_status(e, "gather launch");
+}

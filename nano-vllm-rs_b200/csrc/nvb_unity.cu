@@ -5,3 +5,4 @@
 #include "prefill.cu"
 #include "qkv_rope.cu"
 #include "static_scratch.cu"
+#include "gather.cu"

@@ -8,10 +8,13 @@ Two partitions of the work, one process per GPU over torch.distributed:
 * by kv head (configuration 5, long context): rank r owns kv heads
   [r*kvh_local, (r+1)*kvh_local) of every sequence and the query heads of
   their GQA groups; its cache holds only those kv heads. Each rank runs the
-  split-KV decode on its heads, then one all-gather of the BF16 outputs
-  rebuilds [batch, q_heads, 128] on every rank (`KvHeadShardedDecode`).
-  The transfer is batch * q_heads * 256 B (8 KiB per rank at 4 x 64 heads),
-  so NCCL over NVLink is launch-latency bound; no kernel reads peer memory.
+  split-KV decode on its heads and every rank needs the whole
+  [batch, q_heads, 128] output (`KvHeadShardedDecode`). The transfer is
+  batch * q_heads * 256 B (8 KiB per rank at 4 x 64 heads), so a separate
+  collective is launch-latency bound. The default (`fused=True`) stores each
+  combined result straight into every rank's output from the combine kernel
+  (peer stores over NVLink into CUDA IPC buffers, then an epoch-flag barrier:
+  nvb_paged_decode_gather); `fused=False` keeps the NCCL all-gather.
 
 The reference is single-GPU (its README: no NCCL, MPI or tensor
 parallelism); this module is the B200 build's own.
@@ -68,17 +71,45 @@ def gather_heads(local_out, shard: HeadShard, group=None):
     return buf.view(shard.world, b, ql, d).permute(1, 0, 2, 3).reshape(b, shard.world * ql, d)
 
 
+def exchange_peer_buffers(nvb, shard: HeadShard, ptr, handle, group=None):
+    """All-gathers the ranks' IPC handles and maps the peers' buffers:
+    returns every rank's base pointer in rank order (this rank's own `ptr`
+    at its index)."""
+    import torch.distributed as dist
+
+    handles = [handle]
+    if shard.world > 1:
+        handles = [None] * shard.world
+        dist.all_gather_object(handles, handle, group=group)
+    return [ptr if r == shard.rank else nvb.peer_buffer_open(h) for r, h in enumerate(handles)]
+
+
+class _DeviceArray:
+    """A torch view of device memory the library allocated (CUDA array
+    interface)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": typestr,
+                                         "version": 3, "strides": None}
+
+
 class KvHeadShardedDecode:
-    """Decode over a kv-head-sharded paged cache followed by an NCCL
-    all-gather. `k_local` / `v_local` are this rank's caches
+    """Decode over a kv-head-sharded paged cache, then every rank gets the
+    whole output. `k_local` / `v_local` are this rank's caches
     [num_blocks, block_size, kv_local, 128]; `q_local` is
-    [batch, q_local, 128] (the query heads of this rank's kv heads)."""
+    [batch, q_local, 128] (the query heads of this rank's kv heads).
+    fused=True (default): combine and all-gather in one kernel through peer
+    memory; the returned tensor is one of two output buffers used in turn
+    and stays valid until the call after next. fused=False: NCCL all-gather.
+    Call close() before destroying the process group."""
+
+    FLAG_BYTES = 256
 
     def __init__(self, nvb, shard: HeadShard, *, batch, block_size, table_stride, num_blocks, max_k, device,
-                 num_splits=None, group=None):
+                 num_splits=None, group=None, fused=True):
         import torch
 
-        self.nvb, self.shard, self.group = nvb, shard, group
+        self.nvb, self.shard, self.group, self.fused = nvb, shard, group, fused
         self.batch, self.block_size, self.table_stride = batch, block_size, table_stride
         self.num_blocks, self.max_k = num_blocks, max_k
         sms = torch.cuda.get_device_properties(device).multi_processor_count
@@ -87,6 +118,38 @@ class KvHeadShardedDecode:
         self.lse = torch.empty(batch, shard.q_local, 1, dtype=torch.float32, device=device)
         self.la, self.oa = (nvb.splitkv_scratch(self.splits, batch, shard.q_local, device) if self.splits > 1
                             else (None, None))
+        self.epoch = 0
+        self._own = None
+        self._peers = []
+        if fused:
+            self._setup_peers(device)
+
+    def _setup_peers(self, device):
+        """One IPC-shared device buffer per rank: flags, then two outputs."""
+        import torch
+
+        out_elems = self.batch * self.shard.q_heads * 128
+        self.out_bytes = (out_elems * 2 + 255) // 256 * 256
+        with torch.cuda.device(device):
+            ptr, handle = self.nvb.peer_buffer_create(self.FLAG_BYTES + 2 * self.out_bytes)
+            self._own = ptr
+            bases = exchange_peer_buffers(self.nvb, self.shard, ptr, handle, self.group)
+            self._peers = [b for r, b in enumerate(bases) if r != self.shard.rank]
+        self.flag_ptrs = bases
+        self.out_ptrs = [[b + self.FLAG_BYTES + i * self.out_bytes for b in bases] for i in range(2)]
+        shape = (self.batch, self.shard.q_heads, 128)
+        self.views = [torch.as_tensor(_DeviceArray(ptr + self.FLAG_BYTES + i * self.out_bytes, shape, "<i2"),
+                                      device=device).view(torch.bfloat16) for i in range(2)]
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (fused mode)."""
+        for p in self._peers:
+            self.nvb.peer_buffer_close(p)
+        self._peers = []
+        if self._own is not None:
+            self.views = []
+            self.nvb.peer_buffer_free(self._own)
+            self._own = None
 
     def local(self, q_local, k_local, v_local, cu_q, kv_lens, block_table, check=True):
         self.nvb.paged_fwd(q_local, k_local, v_local, self.out_local, cu_q, kv_lens, block_table, batch=self.batch,
@@ -96,5 +159,16 @@ class KvHeadShardedDecode:
         return self.out_local
 
     def __call__(self, q_local, k_local, v_local, cu_q, kv_lens, block_table, check=True):
-        self.local(q_local, k_local, v_local, cu_q, kv_lens, block_table, check)
-        return gather_heads(self.out_local, self.shard, self.group)
+        if not self.fused:
+            self.local(q_local, k_local, v_local, cu_q, kv_lens, block_table, check)
+            return gather_heads(self.out_local, self.shard, self.group)
+        self.epoch += 1
+        i = self.epoch & 1
+        self.nvb.paged_decode_gather(q_local, k_local, v_local, self.out_local, cu_q, kv_lens, block_table,
+                                     batch=self.batch, max_k=self.max_k, q_heads=self.shard.q_local,
+                                     kv_heads=self.shard.kv_local, block_size=self.block_size,
+                                     table_stride=self.table_stride, num_blocks=self.num_blocks,
+                                     num_splits=self.splits, lse_accum=self.la, out_accum=self.oa,
+                                     peer_out=self.out_ptrs[i], peer_flag=self.flag_ptrs, rank=self.shard.rank,
+                                     epoch=self.epoch, check=check)
+        return self.views[i]

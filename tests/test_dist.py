@@ -109,3 +109,39 @@ def test_shard_plan_rejects_uneven_heads():
         S.HeadShard(0, 3, kv_heads=8, q_heads=64)
     assert [len(S.sequence_shard(256, r, 8)) for r in range(8)] == [32] * 8
     assert sum(len(S.sequence_shard(7, r, 3)) for r in range(3)) == 7
+
+
+class _FakePeerLib:
+    """Stands in for the CUDA IPC calls: a handle is the owner's pointer."""
+
+    def peer_buffer_open(self, handle):
+        return int.from_bytes(handle[:8], "little") + 1  # a mapping differs from the owner's address
+
+
+def _peer_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+        S = _load()
+        shard = S.HeadShard(rank, world, kv_heads=8, q_heads=64)
+        own = 0x1000 * (rank + 1)
+        bases = S.exchange_peer_buffers(_FakePeerLib(), shard, own, own.to_bytes(64, "little"))
+        q.put((rank, bases))
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+def test_peer_buffer_exchange_world2():
+    # each rank keeps its own pointer and maps the other's handle, in rank order
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert results[0] == [0x1000, 0x2000 + 1], results
+    assert results[1] == [0x1000 + 1, 0x2000], results
