@@ -4,14 +4,16 @@
  * `--attention-backend` seam.
  *
  * Every pointer except `stream` is a CUDA device pointer on the current
- * device. `stream` is a cudaStream_t owned by the caller. No entry point
- * allocates device memory, synchronizes the stream, or owns a context, so
- * the launches of the entry points below (nvb_paged_decode_static_scratch
- * aside: see its own comment) are safe inside CUDA-graph stream capture,
- * with one exception: the first launch that sees a new KV-cache base pointer
- * encodes its TMA descriptor on the host (no device work); do that first
- * launch before capture, as the reference engine does with its warm-up
- * forward.
+ * device. `stream` is a cudaStream_t owned by the caller. No attention entry
+ * point allocates device memory, synchronizes the stream, or owns a context,
+ * so their launches (nvb_paged_decode_static_scratch aside: see its own
+ * comment) are safe inside CUDA-graph stream capture, with one exception:
+ * the first launch that sees a new KV-cache base pointer encodes its TMA
+ * descriptor on the host (no device work); do that first launch before
+ * capture, as the reference engine does with its warm-up forward. The
+ * multi-GPU set-up calls nvb_peer_buffer_* allocate and map memory (call
+ * them once, outside capture), and nvb_paged_decode_gather takes a per-call
+ * epoch, so a captured launch would replay a stale one: launch it directly.
  *
  * Layouts (identical to the reference):
  *   q, out           [total_q, q_heads, 128] bf16, contiguous
@@ -144,8 +146,10 @@ const char* nvb_last_error(void);
  * explicit stream instead of the reference's Context*. Row r attends to
  * positions[r] + 1 keys of block-table row seq_indices[r]; rows whose
  * sequence or context is invalid get zero output, as in the reference.
- * head_dim must be 128 and block_size a multiple of 32; other values are
- * rejected with -1. Requires no scratch. */
+ * head_dim 128 (block_size a multiple of 32) runs on the tiled decode;
+ * other head sizes from 1 to 512 (any block size) run on a generic CUDA-core
+ * kernel, as the reference dispatches head sizes (kernels.cu:226-271,
+ * 475-485). Other values are rejected with -1. Requires no scratch. */
 int nvb_attention(void* stream, const void* q, const void* kcache, const void* vcache,
                   const int* positions, const int* seq_indices, const int* tables, void* out,
                   int rows, int q_heads, int kv_heads, int head_dim, int block_size,
@@ -155,7 +159,7 @@ int nvb_attention(void* stream, const void* q, const void* kcache, const void* v
  * research entry `nv_attention_splitkv_candidate`
  * (kernels/decode_candidate.cuh:111-202, 247): (scratch, partitions)
  * appended. scratch holds rows * q_heads * partitions * (128 + 2) floats;
- * 1 <= partitions <= 128. */
+ * 1 <= partitions <= 128; partitions > 1 needs head_dim 128. */
 int nvb_attention_splitkv(void* stream, const void* q, const void* kcache, const void* vcache,
                           const int* positions, const int* seq_indices, const int* tables,
                           void* out, int rows, int q_heads, int kv_heads, int head_dim,

@@ -239,7 +239,18 @@ int native_impl(void* stream, const void* q, const void* kc, const void* vc, con
   if (!q || !kc || !vc || !positions || !seq_indices || !tables || !out || rows <= 0 || qh <= 0 || kvh <= 0 ||
       qh % kvh || bs <= 0 || blocks <= 0 || stride <= 0 || batch <= 0 || max_context <= 0)
     return fail("invalid paged attention arguments");
-  if (dim != 128) return fail("only head_dim 128 is supported (got %d)", dim);
+  if (dim != 128) {
+    // Other head sizes (kernels/kernels.cu:475-485 dispatch, generic kernel
+    // kernels.cu:226-271): the CUDA-core path of generic.cu.
+    if (dim < 1 || dim > 512) return fail("head_dim must be in [1, 512] (got %d)", dim);
+    if (partitions != 1) return fail("split partitions are supported for head_dim 128 only");
+    if ((long long)blocks * bs > INT_MAX) return fail("num_blocks * block_size must fit in int32");
+    if ((long long)stride * bs > INT_MAX) return fail("table_stride * block_size must fit in int32");
+    return cuda_status(launch_generic_attention(q, kc, vc, out, positions, seq_indices, tables, rows, qh, kvh, dim,
+                                                bs, blocks, stride, batch, max_context,
+                                                static_cast<cudaStream_t>(stream)),
+                       "generic attention launch");
+  }
   if (bs % 32) return fail("block_size must be a multiple of 32 (got %d)", bs);
   if ((long long)blocks * bs > INT_MAX) return fail("num_blocks * block_size must fit in int32");
   if (qh / kvh > 16) return fail("at most 16 query heads per kv head are supported");

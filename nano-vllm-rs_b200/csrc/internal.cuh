@@ -71,4 +71,10 @@ int make_map_3d(const void* base, const uint64_t dims[3], const uint64_t strides
 // Returns cudaErrorNotSupported when the tcgen05 path does not cover the shape.
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
 
+// Native-form attention for head dimensions other than 128 (generic.cu).
+cudaError_t launch_generic_attention(const void* q, const void* k, const void* v, void* out, const int* positions,
+                                     const int* seq_indices, const int* tables, int rows, int qh, int kvh, int dim,
+                                     int block_size, int num_blocks, int table_stride, int batch, int max_context,
+                                     cudaStream_t stream);
+
 }  // namespace nvb

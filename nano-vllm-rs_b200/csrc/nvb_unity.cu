@@ -6,3 +6,4 @@
 #include "qkv_rope.cu"
 #include "static_scratch.cu"
 #include "gather.cu"
+#include "generic.cu"

@@ -68,9 +68,10 @@ def test_native_entry_rejects_unsupported_shapes_on_host(nvb):
     lib = nvb.library()
     P = ctypes.c_void_p
     nz = P(256)
-    # head_dim 64, block_size 2 (the reference supports them; this library does not)
-    assert lib.nvb_attention(P(0), nz, nz, nz, nz, nz, nz, nz, 4, 4, 2, 64, 256, 4, 2, 2, 4096) == -1
-    assert b"head_dim 128" in lib.nvb_last_error()
+    # head_dim beyond 512; block_size 2 at head_dim 128 (other head sizes run on
+    # the generic path, which takes any block size)
+    assert lib.nvb_attention(P(0), nz, nz, nz, nz, nz, nz, nz, 4, 4, 2, 600, 256, 4, 2, 2, 4096) == -1
+    assert b"head_dim must be in [1, 512]" in lib.nvb_last_error()
     assert lib.nvb_attention(P(0), nz, nz, nz, nz, nz, nz, nz, 4, 4, 2, 128, 2, 4, 2, 2, 4096) == -1
     assert b"multiple of 32" in lib.nvb_last_error()
     assert lib.nvb_qkv_rope_cached(P(0), nz, nz, nz, nz, nz, nz, nz, nz, 1, 4, 2, 128, 256, 1, ctypes.c_float(0.0),
