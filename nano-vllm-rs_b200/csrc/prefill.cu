@@ -91,7 +91,10 @@ constexpr int kItemOff = 320;                               // Item [2] (the pub
 constexpr int kItemBytes = 64;
 constexpr int kStatsOff = 512;                              // float2 [128]: row max used, row sum
 constexpr int kXOff = kStatsOff + kRows * 8;                // float [2 slots][2 halves][128]
-constexpr int kHeadBytes = kXOff + 2 * 2 * kRows * 4;
+constexpr int kMaxSorted = 1024;                            // batches up to this size are claimed by work
+constexpr int kOrderOff = kXOff + 2 * 2 * kRows * 4;        // int [kMaxSorted]: sequences, heaviest first
+constexpr int kWorkOff = kOrderOff + kMaxSorted * 4;        // float [kMaxSorted]: each sequence's work
+constexpr int kHeadBytes = kWorkOff + kMaxSorted * 4;
 constexpr int kQOff = 0;                                    // offsets from the 1 KB aligned tile base
 constexpr int kKOff = kQOff + kQStages * kQBytes;
 constexpr int kVOff = kKOff + kKStages * kKVBytes;
@@ -250,8 +253,9 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
 // One 128-row query tile of one (sequence, kv head): the work item of the
 // persistent loop. Virtual items are grouped by (sequence, kv head), longest
 // causal tile first within a group, so the CTAs running at one time share a
-// few groups' K/V in L2; CTAs claim items from a global counter (dynamic load
-// balancing), so an SM that drew short items takes more of them.
+// few groups' K/V in L2; the sequences come heaviest first (ranked at kernel
+// start for batches up to kMaxSorted) and CTAs claim items from a global
+// counter (dynamic load balancing), so the last claims are small ones.
 struct Item {
   int b, h, q_begin, q0, kv_len, prefix;
   int qx;       // queries in the tile
@@ -261,12 +265,14 @@ struct Item {
 };
 static_assert(sizeof(Item) <= kItemBytes, "item ring slot too small");
 
-__device__ __forceinline__ Item make_item(const PrefillParams& p, int v) {
+// `order` (or null): sequence of each rank, heaviest first.
+__device__ __forceinline__ Item make_item(const PrefillParams& p, const int* order, int v) {
   Item it;
   const int group = v / p.n_qtiles;
   const int tile = p.n_qtiles - 1 - (v - group * p.n_qtiles);
-  it.b = group / p.kvh;
-  it.h = group - it.b * p.kvh;
+  const int rank = group / p.kvh;
+  it.b = order ? order[rank] : rank;
+  it.h = group - rank * p.kvh;
   it.q_begin = p.cu_q[it.b];
   const int q_len = p.cu_q[it.b + 1] - it.q_begin;
   it.q0 = tile * p.qt;
@@ -365,6 +371,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_proxy_async_smem();
   }
+  // Sequences ranked by their work (about q tiles x keys seen), heaviest
+  // first, so that dynamic claiming ends with small items (the rank of each
+  // sequence is the count of heavier ones; ties by index).
+  int* order = nullptr;
+  if (p.batch <= kMaxSorted) {
+    order = reinterpret_cast<int*>(head + kOrderOff);
+    float* work = reinterpret_cast<float*>(head + kWorkOff);
+    for (int b = threadIdx.x; b < p.batch; b += kThreads) {
+      const int q_len = p.cu_q[b + 1] - p.cu_q[b];
+      const int prefix = p.kv_lens[b] - q_len;
+      work[b] = (q_len > 0 && prefix >= 0)
+                    ? float((q_len + p.qt - 1) / p.qt) * (float(prefix) + 0.5f * float(q_len) + float(p.qt))
+                    : 0.0f;
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < p.batch; b += kThreads) {
+      const float wb = work[b];
+      int rank = 0;
+      for (int j = 0; j < p.batch; ++j) rank += (work[j] > wb) || (work[j] == wb && j < b);
+      order[rank] = b;
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -385,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         do {
           v = atomicAdd(p.sched, 1);
           if (v >= n_items) break;
-          it = make_item(p, v);
+          it = make_item(p, order, v);
           if (it.qx == 0) {
             // Tiles past the sequence's queries come first in their group:
             // move the counter to the group's last (non-empty) tile if nobody
