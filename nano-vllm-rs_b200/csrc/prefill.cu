@@ -77,11 +77,11 @@ constexpr float kRescaleLog2 = 8.0f;         // lazy rescale threshold (P <= 2^8
 
 enum Bar {
   kQFull = 0, kQFree = 2, kKFull = 4, kKEmpty = 6, kVFull = 8, kVFixed = 10, kVEmpty = 12,  // [2]
-  kSFull = 14, kPVDone = 17,                                                               // [3]: per S buffer
-  kPFull = 20, kODone = 21, kOFree = 22, kStatsFull = 23, kStatsFree = 24,
-  kXchg = 25,                                                                              // [4]: per TMEM quadrant
-  kItemFull = 29, kItemEmpty = 31,                                                         // [2]
-  kDrain = 33, kNumBars = 34
+  kSFull = 14, kPVDone = 17, kPFull = 20,                                                  // [3]: per S buffer
+  kODone = 23, kOFree = 24, kStatsFull = 25, kStatsFree = 26,
+  kXchg = 27,                                                                              // [4]: per TMEM quadrant
+  kItemFull = 31, kItemEmpty = 33,                                                         // [2]
+  kDrain = 35, kNumBars = 36
 };
 // Readers of each published item: V producer, MMA issuer, V fixer (one
 // arrival each) and the 8 softmax + 4 epilogue warps (one per warp).
@@ -343,10 +343,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < kSBufs; ++b) {
       mbar_init(&bars[kSFull + b], 1);
       mbar_init(&bars[kPVDone + b], 1);
+      mbar_init(&bars[kPFull + b], 8);
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q) mbar_init(&bars[kXchg + q], 64);
-    mbar_init(&bars[kPFull], 8);
     mbar_init(&bars[kODone], 1);
     mbar_init(&bars[kOFree], 4);
     mbar_init(&bars[kStatsFull], kRows);
@@ -516,13 +516,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int gt = 0, ix = 0;  // tiles and items (with keys) so far
       bool alive = true;
-      // O += P_t V_t. Waits for the fixer's V, the softmax's P and, for the
-      // item's first tile, the epilogue's read of the previous O.
-      auto issue_pv = [&](int t, bool first, bool last) -> bool {
+      // O += P_t V_t for item `item`. Waits for the fixer's V, the softmax's
+      // P and, for the item's first tile, the epilogue's read of the previous
+      // item's O.
+      auto issue_pv = [&](int t, bool first, bool last, int item) -> bool {
         const int vs = t & 1, buf = t % kSBufs;
         if (!mbar_wait(&bars[kVFixed + vs], (t >> 1) & 1, kErrPrefillWait)) return false;
-        if (first && ix > 0 && !mbar_wait(&bars[kOFree], (ix - 1) & 1, kErrPrefillWait)) return false;
-        if (!mbar_wait(&bars[kPFull], t & 1, kErrPrefillWait)) return false;
+        if (first && item > 0 && !mbar_wait(&bars[kOFree], (item - 1) & 1, kErrPrefillWait)) return false;
+        if (!mbar_wait(&bars[kPFull + buf], (t / kSBufs) & 1, kErrPrefillWait)) return false;
         tc_fence_after();
         const uint32_t v_addr = sbase + kVOff + vs * kKVBytes;
 #pragma unroll
@@ -536,6 +537,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (last) umma_commit(&bars[kODone]);
         return true;
       };
+      // The S/PV interleave S_t, PV_{t-1}, S_{t+1}, PV_t, ... runs on across
+      // items: the last PV of an item is issued after the next item's first
+      // S (owed_t), so the softmax finds the next scores ready when it
+      // finishes an item.
+      int owed_t = -1, owed_ix = 0;
+      bool owed_first = false;
       Item it;
       for (int i = 0; alive && take_item(bars, ring, i, false, it); ++i) {
         if (it.n == 0) continue;
@@ -560,13 +567,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&bars[kSFull + buf]);
           umma_commit(&bars[kKEmpty + ks]);
           if (j == it.n - 1) umma_commit(&bars[kQFree + qs]);
-          if (j >= 1) alive = issue_pv(t - 1, j == 1, false);
+          if (j >= 1) {
+            alive = issue_pv(t - 1, j == 1, false, ix);
+          } else if (owed_t >= 0) {
+            alive = issue_pv(owed_t, owed_first, true, owed_ix);
+            owed_t = -1;
+          }
         }
-        if (alive) alive = issue_pv(gt + it.n - 1, it.n == 1, true);
         if (!alive) break;
+        owed_t = gt + it.n - 1;
+        owed_first = it.n == 1;
+        owed_ix = ix;
         ++ix;
         gt += it.n;
       }
+      if (alive && owed_t >= 0) issue_pv(owed_t, owed_first, true, owed_ix);
       // every MMA issued by this thread completes before TMEM is freed
       umma_commit(&bars[kDrain]);
       mbar_wait(&bars[kDrain], 0, kErrPrefillWait);
@@ -706,16 +721,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         // keys [64 hf, +64) -> packed columns [32 hf, +32) of this buffer
         tmem_st32(scol + hf * 32, pk);
         l = l * alpha + (((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7])));
-        // O is quiescent once PV_{t-1} has completed (PV_t waits for this P).
-        if (t >= 1) {
+        if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+          // O is quiescent once PV_{t-1} has completed (PV_t waits for this
+          // P). Waited on only here: the issuer waited for PV_{t-3} before
+          // S_t, and PV_{t+2} needs this warp's P, so the barrier of buffer
+          // (t-1) % kSBufs is at PV_{t-1}'s phase or one past it.
           const int pb = (t - 1) % kSBufs;
           if (!warp_wait(&bars[kPVDone + pb], ((t - 1) / kSBufs) & 1)) {
             alive = false;
             break;
           }
           tc_fence_after();
-        }
-        if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
           // this half rescales O columns [64 hf, +64)
           uint32_t o0[32], o1[32];
           const uint32_t oaddr = lane_base + kOCol + hf * 64;
@@ -733,7 +749,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[kPFull]);
+        // One P barrier per S buffer: P_{t+3} needs S_{t+3}, hence PV_t, so
+        // the issuer is never two phases behind it.
+        if (lane == 0) mbar_arrive(&bars[kPFull + buf]);
       }
       if (!alive) break;
       // Row sum = both halves' sums; half 0 hands (max used, sum) to the
