@@ -152,6 +152,29 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Division by an invariant positive divisor d with one multiply-high, after
+// Granlund and Montgomery, "Division by invariant integers using
+// multiplication" (PLDI 1994), figure 4.1: with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (mulhi(m, n) + n) >> l for every
+// 32-bit unsigned n. Integer division by a value known only at run time
+// otherwise goes through the MUFU reciprocal, which the softmax of the
+// attention kernels keeps saturated with exponentials.
+struct FastDiv {
+  uint32_t m = 1, l = 0;
+  int d = 1;
+  static FastDiv make(int divisor) {
+    FastDiv f;
+    f.d = divisor;
+    while ((1ull << f.l) < uint64_t(divisor)) ++f.l;
+    f.m = uint32_t(((uint64_t(1) << 32) * ((uint64_t(1) << f.l) - uint64_t(divisor))) / uint64_t(divisor) + 1);
+    return f;
+  }
+  // n >= 0
+  __device__ __forceinline__ int div(int n) const {
+    return int((uint64_t(__umulhi(m, uint32_t(n))) + uint32_t(n)) >> l);
+  }
+};
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -113,6 +113,7 @@ struct PrefillParams {
   int batch, max_q, qh, kvh, group, qt, rows_used, block_size, table_stride, num_blocks;
   float scale_log2;
   int* sched;  // {next item to claim, CTAs finished}: zero at launch, reset by the last CTA
+  FastDiv fd_nqt, fd_kvh, fd_qt, fd_bs;  // by n_qtiles, kvh, qt, block_size
 };
 
 // ------------------------------------------------------------- tcgen05 PTX
@@ -134,24 +135,31 @@ constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 4
 constexpr uint32_t kIdescS = kIdescBase;
 constexpr uint32_t kIdescPV = kIdescBase | (1u << 16);
 
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// D (+)= A B with A and B from shared memory (umma_ss) or A from TMEM
+// (umma_ts); each shared-memory descriptor is passed as its (low, high)
+// words. The issuer builds every descriptor once and moves between
+// stages and K16 steps by adding (byte offset >> 4) to the low word: the start
+// address field is bits 0-13 and shared addresses stay below 2^18, so the add
+// never carries out of it. This keeps the one issuing thread, which shares
+// its SMSP with two softmax warps, at a few instructions per MMA.
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
+                                        uint32_t idesc, uint32_t acc) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\tsetp.ne.b32 p, %6, 0;\n\t"
+      "mov.b64 da, {%1, %2};\n\tmov.b64 db, {%3, %4};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(acc)
       : "memory");
 }
-
-// O += P V with A (P, packed BF16 pairs) read from tensor memory.
-__device__ __forceinline__ void umma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                                 uint32_t acc) {
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
+                                        uint32_t acc) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\tsetp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(acc)
       : "memory");
 }
-
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                : "memory");
@@ -268,9 +276,9 @@ static_assert(sizeof(Item) <= kItemBytes, "item ring slot too small");
 // `order` (or null): sequence of each rank, heaviest first.
 __device__ __forceinline__ Item make_item(const PrefillParams& p, const int* order, int v) {
   Item it;
-  const int group = v / p.n_qtiles;
+  const int group = p.fd_nqt.div(v);
   const int tile = p.n_qtiles - 1 - (v - group * p.n_qtiles);
-  const int rank = group / p.kvh;
+  const int rank = p.fd_kvh.div(group);
   it.b = order ? order[rank] : rank;
   it.h = group - rank * p.kvh;
   it.q_begin = p.cu_q[it.b];
@@ -382,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q_len = p.cu_q[b + 1] - p.cu_q[b];
       const int prefix = p.kv_lens[b] - q_len;
       work[b] = (q_len > 0 && prefix >= 0)
-                    ? float((q_len + p.qt - 1) / p.qt) * (float(prefix) + 0.5f * float(q_len) + float(p.qt))
+                    ? float(p.fd_qt.div(q_len + p.qt - 1)) * (float(prefix) + 0.5f * float(q_len) + float(p.qt))
                     : 0.0f;
     }
     __syncthreads();
@@ -419,8 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             // move the counter to the group's last (non-empty) tile if nobody
             // has claimed past this one yet.
             const int q_len = p.cu_q[it.b + 1] - it.q_begin;
-            const int tiles = (q_len + p.qt - 1) / p.qt;
-            const int group_end = (v / p.n_qtiles + 1) * p.n_qtiles;
+            const int tiles = q_len > 0 ? p.fd_qt.div(q_len + p.qt - 1) : 0;
+            const int group_end = (p.fd_nqt.div(v) + 1) * p.n_qtiles;
             atomicCAS(p.sched, v + 1, group_end - tiles);
           }
         } while (it.qx == 0);
@@ -446,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < it.n; ++j) {
           const int g = gt + j, st = g & 1;
           const int key0 = j * kKeys;
-          const int logical = key0 / p.block_size;
+          const int logical = p.fd_bs.div(key0);
           const int page = table[logical];
           const bool ok = page_ok(page, p.num_blocks);
           const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
@@ -487,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < it.n; ++j) {
           const int g = gt + j, st = g & 1;
           const int key0 = j * kKeys;
-          const int logical = key0 / p.block_size;
+          const int logical = p.fd_bs.div(key0);
           const int page = table[logical];
           const bool ok = page_ok(page, p.num_blocks);
           const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
@@ -516,6 +524,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int gt = 0, ix = 0;  // tiles and items (with keys) so far
       bool alive = true;
+      // Descriptors of stage 0 of Q, K and V; stages are 2048 16-byte units apart.
+      const uint64_t qd = sw128_desc(sbase + kQOff, 16, 1024), kd = sw128_desc(sbase + kKOff, 16, 1024);
+      const uint64_t vd = sw128_desc(sbase + kVOff, kHalf, 1024);
+      const uint32_t q_lo = uint32_t(qd), q_hi = uint32_t(qd >> 32), k_lo = uint32_t(kd), k_hi = uint32_t(kd >> 32);
+      const uint32_t v_lo = uint32_t(vd), v_hi = uint32_t(vd >> 32);
+      static_assert(kQBytes == kKVBytes && kKVBytes >> 4 == 2048, "stage stride in descriptor units");
       // O += P_t V_t for item `item`. Waits for the fixer's V, the softmax's
       // P and, for the item's first tile, the epilogue's read of the previous
       // item's O.
@@ -525,12 +539,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (first && item > 0 && !mbar_wait(&bars[kOFree], (item - 1) & 1, kErrPrefillWait)) return false;
         if (!mbar_wait(&bars[kPFull + buf], (t / kSBufs) & 1, kErrPrefillWait)) return false;
         tc_fence_after();
-        const uint32_t v_addr = sbase + kVOff + vs * kKVBytes;
+        const uint32_t vb = v_lo + uint32_t(vs) * 2048u, pa = tmem + buf * kKeys;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           // P: 16 keys = 8 packed columns; V: 16 keys = 2048 bytes of rows
-          umma_bf16_tmem_a(tmem + kOCol, tmem + buf * kKeys + kk * 8, sw128_desc(v_addr + kk * 2048, kHalf, 1024),
-                           kIdescPV, (!first || kk > 0) ? 1u : 0u);
+          umma_ts(tmem + kOCol, pa + kk * 8, vb + kk * 128, v_hi, kIdescPV, (!first || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars[kPVDone + buf]);
         umma_commit(&bars[kVEmpty + vs]);
@@ -547,7 +560,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; alive && take_item(bars, ring, i, false, it); ++i) {
         if (it.n == 0) continue;
         const int qs = ix & 1;
-        const uint32_t q_addr = sbase + kQOff + qs * kQBytes;
         for (int j = 0; j < it.n && alive; ++j) {
           const int t = gt + j, ks = t & 1, buf = t % kSBufs;
           alive = mbar_wait(&bars[kKFull + ks], (t >> 1) & 1, kErrPrefillWait);
@@ -557,12 +569,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             alive = mbar_wait(&bars[kPVDone + buf], ((t - kSBufs) / kSBufs) & 1, kErrPrefillWait);
           if (!alive) break;
           tc_fence_after();
-          const uint32_t k_addr = sbase + kKOff + ks * kKVBytes;
+          const uint32_t qa = q_lo + uint32_t(qs) * 2048u, kb = k_lo + uint32_t(ks) * 2048u, sd = tmem + buf * kKeys;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-            umma_bf16(tmem + buf * kKeys, sw128_desc(q_addr + off, 16, 1024), sw128_desc(k_addr + off, 16, 1024),
-                      kIdescS, kk > 0 ? 1u : 0u);
+            const uint32_t off = uint32_t((kk >> 2) * kHalf + (kk & 3) * 32) >> 4;
+            umma_ss(sd, qa + off, q_hi, kb + off, k_hi, kIdescS, kk > 0 ? 1u : 0u);
           }
           umma_commit(&bars[kSFull + buf]);
           umma_commit(&bars[kKEmpty + ks]);
@@ -597,7 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < it.n; ++j) {
         const int g = gt + j, st = g & 1;
         const int key0 = j * kKeys;
-        const bool ok = page_ok(table[key0 / p.block_size], p.num_blocks);
+        const bool ok = page_ok(table[p.fd_bs.div(key0)], p.num_blocks);
         const int real = ok ? min(kKeys, it.kv_len - key0) : 0;
         if (!warp_wait(&bars[kVFull + st], (g >> 1) & 1)) {
           alive = false;
@@ -646,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < it.n; ++j, ++t) {
         const int buf = t % kSBufs;
         const int key0 = j * kKeys;
-        const bool ok = page_ok(table[key0 / p.block_size], p.num_blocks);
+        const bool ok = page_ok(table[p.fd_bs.div(key0)], p.num_blocks);
         if (!warp_wait(&bars[kSFull + buf], (t / kSBufs) & 1)) {
           alive = false;
           break;
@@ -778,7 +789,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
       const int qpos = it.q0 + rq;
       const bool valid_row = r < p.rows_used && rq < it.qx && qpos < p.max_q;
-      const int head = it.h * p.group + (r % p.group);
+      const int head = it.h * p.group + (r - rq * p.group);
       __nv_bfloat16* dst = p.out + (((long long)it.q_begin + qpos) * p.qh + head) * 128;
       float* lse_dst = p.lse ? p.lse + ((long long)it.b * p.qh + head) * p.max_q + qpos : nullptr;
       if (it.n == 0) {
@@ -934,6 +945,10 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   p.sched = sched_pair(stream, dev, &e);
   if (!p.sched) return e;
   p.n_qtiles = (a.max_q + qt - 1) / qt;
+  p.fd_nqt = FastDiv::make(p.n_qtiles > 0 ? p.n_qtiles : 1);
+  p.fd_kvh = FastDiv::make(a.kvh);
+  p.fd_qt = FastDiv::make(qt);
+  p.fd_bs = FastDiv::make(a.block_size);
   const long long items = (long long)p.n_qtiles * a.batch * a.kvh;
   if (items > 0x7fffffffLL) return cudaErrorNotSupported;
   const int grid = int(items < sm_count[dev & 63] ? items : sm_count[dev & 63]);
