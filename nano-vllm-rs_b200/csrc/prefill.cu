@@ -76,7 +76,7 @@ constexpr float kLn2 = 0.693147180559945309f;
 constexpr float kRescaleLog2 = 8.0f;         // lazy rescale threshold (P <= 2^8)
 
 enum Bar {
-  kQFull = 0, kQFree = 2, kKFull = 4, kKEmpty = 6, kVFull = 8, kVFixed = 10, kVEmpty = 12,  // [2]
+  kQFull = 0, kQFree = 2, kKFull = 4, kKEmpty = 6, kVFull = 8, kPVDrain = 10, kVEmpty = 12,  // [2]
   kSFull = 14, kPVDone = 17, kPFull = 20,                                                  // [3]: per S buffer
   kODone = 23, kOFree = 24, kStatsFull = 25, kStatsFree = 26,
   kXchg = 27,                                                                              // [4]: per TMEM quadrant
@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars[kKFull + s], 1);
       mbar_init(&bars[kKEmpty + s], 1);
       mbar_init(&bars[kVFull + s], 1);
-      mbar_init(&bars[kVFixed + s], 1);
+      mbar_init(&bars[kPVDrain + s], 1);
       mbar_init(&bars[kVEmpty + s], 1);
       mbar_init(&bars[kItemFull + s], 1);
       mbar_init(&bars[kItemEmpty + s], kItemReaders);
@@ -526,36 +526,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool alive = true;
       // Descriptors of stage 0 of Q, K and V; stages are 2048 16-byte units apart.
       const uint64_t qd = sw128_desc(sbase + kQOff, 16, 1024), kd = sw128_desc(sbase + kKOff, 16, 1024);
-      const uint64_t vd = sw128_desc(sbase + kVOff, kHalf, 1024);
       const uint32_t q_lo = uint32_t(qd), q_hi = uint32_t(qd >> 32), k_lo = uint32_t(kd), k_hi = uint32_t(kd >> 32);
-      const uint32_t v_lo = uint32_t(vd), v_hi = uint32_t(vd >> 32);
       static_assert(kQBytes == kKVBytes && kKVBytes >> 4 == 2048, "stage stride in descriptor units");
-      // O += P_t V_t for item `item`. Waits for the fixer's V, the softmax's
-      // P and, for the item's first tile, the epilogue's read of the previous
-      // item's O.
-      auto issue_pv = [&](int t, bool first, bool last, int item) -> bool {
-        const int vs = t & 1, buf = t % kSBufs;
-        if (!mbar_wait(&bars[kVFixed + vs], (t >> 1) & 1, kErrPrefillWait)) return false;
-        if (first && item > 0 && !mbar_wait(&bars[kOFree], (item - 1) & 1, kErrPrefillWait)) return false;
-        if (!mbar_wait(&bars[kPFull + buf], (t / kSBufs) & 1, kErrPrefillWait)) return false;
-        tc_fence_after();
-        const uint32_t vb = v_lo + uint32_t(vs) * 2048u, pa = tmem + buf * kKeys;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          // P: 16 keys = 8 packed columns; V: 16 keys = 2048 bytes of rows
-          umma_ts(tmem + kOCol, pa + kk * 8, vb + kk * 128, v_hi, kIdescPV, (!first || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&bars[kPVDone + buf]);
-        umma_commit(&bars[kVEmpty + vs]);
-        if (last) umma_commit(&bars[kODone]);
-        return true;
-      };
-      // The S/PV interleave S_t, PV_{t-1}, S_{t+1}, PV_t, ... runs on across
-      // items: the last PV of an item is issued after the next item's first
-      // S (owed_t), so the softmax finds the next scores ready when it
-      // finishes an item.
-      int owed_t = -1, owed_ix = 0;
-      bool owed_first = false;
       Item it;
       for (int i = 0; alive && take_item(bars, ring, i, false, it); ++i) {
         if (it.n == 0) continue;
@@ -578,29 +550,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&bars[kSFull + buf]);
           umma_commit(&bars[kKEmpty + ks]);
           if (j == it.n - 1) umma_commit(&bars[kQFree + qs]);
-          if (j >= 1) {
-            alive = issue_pv(t - 1, j == 1, false, ix);
-          } else if (owed_t >= 0) {
-            alive = issue_pv(owed_t, owed_first, true, owed_ix);
-            owed_t = -1;
-          }
         }
         if (!alive) break;
-        owed_t = gt + it.n - 1;
-        owed_first = it.n == 1;
-        owed_ix = ix;
         ++ix;
         gt += it.n;
       }
-      if (alive && owed_t >= 0) issue_pv(owed_t, owed_first, true, owed_ix);
       // every MMA issued by this thread completes before TMEM is freed
       umma_commit(&bars[kDrain]);
       mbar_wait(&bars[kDrain], 0, kErrPrefillWait);
     }
   } else if (warp == 2) {
-    // ---------------------------------------------------------- V fixer
-    int gt = 0;
+    // ------------------------------------------- V fixer and PV issuer
+    // Fixes V_t, then lane 0 issues O += P_t V_t (the S MMAs come from warp
+    // 1: two issuing threads, so neither stream waits behind the other's
+    // barriers). The item's first PV also waits for the epilogue's read of the
+    // previous item's O.
+    int gt = 0, ix = 0;
     bool alive = true;
+    const uint64_t vd = sw128_desc(sbase + kVOff, kHalf, 1024);
+    const uint32_t v_lo = uint32_t(vd), v_hi = uint32_t(vd >> 32);
     Item it;
     for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
       if (it.n == 0) continue;
@@ -623,9 +591,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[kVFixed + st]);
+        bool ok_pv = true;
+        if (lane == 0) {
+          const int buf = g % kSBufs;
+          if (j == 0 && ix > 0) ok_pv = mbar_wait(&bars[kOFree], (ix - 1) & 1, kErrPrefillWait);
+          if (ok_pv) ok_pv = mbar_wait(&bars[kPFull + buf], (g / kSBufs) & 1, kErrPrefillWait);
+          if (ok_pv) {
+            tc_fence_after();
+            const uint32_t vb = v_lo + uint32_t(st) * 2048u, pa = tmem + buf * kKeys;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              // P: 16 keys = 8 packed columns; V: 16 keys = 2048 bytes of rows
+              umma_ts(tmem + kOCol, pa + kk * 8, vb + kk * 128, v_hi, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(&bars[kPVDone + buf]);
+            umma_commit(&bars[kVEmpty + st]);
+            if (j == it.n - 1) umma_commit(&bars[kODone]);
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, ok_pv, 0)) {
+          alive = false;
+          break;
+        }
       }
+      ++ix;
       gt += it.n;
+    }
+    if (lane == 0) {
+      // every PV MMA completes before TMEM is freed
+      umma_commit(&bars[kPVDrain]);
+      mbar_wait(&bars[kPVDrain], 0, kErrPrefillWait);
     }
   } else if (warp < 12) {
     // ---------------------------------------------------------- softmax
