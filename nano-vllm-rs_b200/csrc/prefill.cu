@@ -24,7 +24,8 @@
 // issued as soon as PV_{t-2} has released its buffer, so the tensor core
 // computes the next scores while the softmax works on the current ones and
 // the per-tile work of the tensor core (1024 cycles at M=N=K=128) overlaps the
-// softmax (~1000-1300 cycles, bounded by the 16-per-clock MUFU unit).
+// softmax (~2,000 cycles a tile for the two warps of an SMSP, of which the
+// exponentials take ~1,100 on the 16-per-clock MUFU unit).
 //
 // Roles (16 warps, one CTA per SM):
 //   warp 0      claims items (global counter, heaviest first), publishes each
@@ -32,10 +33,12 @@
 //               the K tiles (two-stage ring) with TMA: 3-D maps over [tokens,
 //               kv_heads, 128], 64-element 128-byte-swizzled boxes; a 128-key
 //               tile never crosses a page since block_size is a multiple of 256
-//   warp 1      TMEM owner; one thread issues every MMA and commit
-//   warp 2      V fixer: zeroes V rows that are not real keys (past kv_len or an
-//               invalid page) so P ~ 0 never meets a non-finite cache value,
-//               then releases the tile to the MMA
+//   warp 1      TMEM owner; one thread issues the S MMAs and their commits
+//   warp 2      V fixer and PV issuer: zeroes V rows that are not real keys
+//               (past kv_len or an invalid page) so P ~ 0 never meets a
+//               non-finite cache value, then one thread issues that tile's
+//               PV MMAs once P is in TMEM (two issuing threads: neither the
+//               S nor the PV stream waits behind the other's barriers)
 //   warp 3      loads the V tiles (two-stage ring)
 //   warps 4-7   softmax of keys 0-63 of each tile; warps 8-11 keys 64-127. The
 //               two halves of a row agree on its max through shared memory and
