@@ -14,9 +14,11 @@ Multi-GPU runs are weak-scaled: each rank decodes its own 256-sequence shard
            the step's inputs (new-token QKV projections, positions, slots,
            page tables, kv_lens) go H2D from pinned memory, the fused
            norm/RoPE/KV-store kernel writes the new token into the cache,
-           decode attention runs, and the output comes back D2H. The step
-           is pipelined over sequence chunks (--e2e-chunks) so that one
-           chunk's copies overlap another's kernels.
+           decode attention runs, and the output comes back D2H, on three
+           streams (a step's download overlaps the next step's upload). It
+           can also be pipelined over sequence chunks (--e2e-chunks,
+           --e2e-split) so that one chunk's copies overlap another's
+           kernels; one chunk measured fastest.
   prefill  varlen causal prefill TFLOP/s on BASELINE config 2 (32 prompts,
            lengths U[64, 2048], 16q/8kv), causal FLOPs of visible keys only.
 
@@ -271,8 +273,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--e2e-chunks", type=int, default=2,
+    ap.add_argument("--e2e-chunks", type=int, default=1,
                     help="sequence chunks the end-to-end step is pipelined over (copies overlap compute)")
+    ap.add_argument("--e2e-split", type=str, default=None,
+                    help="comma-separated chunk sizes in sequences (sum = batch); overrides --e2e-chunks")
     ap.add_argument("--no-long-context", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 256 = config 3; smaller only for profiler captures)")
@@ -350,6 +354,7 @@ def main():
 
     # ---------------- end to end through the public API, host buffers
     e2e_value = e2e_ms = None
+    e2e_sizes = None
     h2d = d2h = 0
     e2e_steps = 1
     if not args.no_e2e:
@@ -381,8 +386,17 @@ def main():
         # Step k+1's uploads wait for step k's compute (the next token's
         # projections depend on this step), and its compute waits for step
         # k's downloads (the output buffer is reused).
-        nch = max(1, min(args.e2e_chunks, batch))
-        bounds = [(c * batch // nch, (c + 1) * batch // nch) for c in range(nch)]
+        if args.e2e_split:
+            sizes = [int(x) for x in args.e2e_split.split(",")]
+            if sum(sizes) != batch or min(sizes) < 1:
+                raise SystemExit(f"--e2e-split sizes must be positive and sum to the batch ({batch})")
+            starts = [sum(sizes[:c]) for c in range(len(sizes))]
+            bounds = [(a, a + n) for a, n in zip(starts, sizes)]
+        else:
+            nch = max(1, min(args.e2e_chunks, batch))
+            bounds = [(c * batch // nch, (c + 1) * batch // nch) for c in range(nch)]
+        nch = len(bounds)
+        e2e_sizes = [b - a for a, b in bounds]
         h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
         chunk_cfg = []
         for s0, s1 in bounds:
@@ -524,7 +538,7 @@ def main():
             "long_context": long_ctx,
             "e2e": None if e2e_value is None else {
                 "value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(e2e_ms / e2e_steps, 5), "chunks": nch,
+                "ms_per_step": round(e2e_ms / e2e_steps, 5), "chunks": nch, "chunk_sizes": e2e_sizes,
                 "path": "per sequence chunk: pinned H2D of step inputs -> nvb_qkv_rope_cached -> nvb_paged_fwd_ex -> "
                         "D2H output, chunks pipelined on H2D / compute / D2H streams"},
             "gpu_launches": args.steps * (1 if splits == 1 else 2),
