@@ -369,14 +369,32 @@ def main():
                                    dtype=torch.int32))
         table_h, lens_h, cuq_h = pin(case.block_table), pin(case.kv_lens), pin(case.cu_q)
         out_h = torch.empty(batch, QH, DIM, dtype=torch.bfloat16).pin_memory()
-        dev_in = {n: torch.empty_like(t, device=dev) for n, t in
-                  (("qkv", qkv_h), ("pos", positions_h), ("slots", slots_h), ("table", table_h), ("lens", lens_h),
-                   ("cuq", cuq_h))}
-        host_in = {"qkv": qkv_h, "pos": positions_h, "slots": slots_h, "table": table_h, "lens": lens_h, "cuq": cuq_h}
+        # All step inputs live in one pinned staging buffer with the same
+        # layout on the device (the step metadata first, then the QKV rows;
+        # 256-byte aligned fields), so a step uploads with one copy (or one
+        # per chunk), as the engine uploads its packed metadata.
+        src = {"pos": positions_h, "slots": slots_h, "table": table_h, "lens": lens_h, "cuq": cuq_h, "qkv": qkv_h}
+        offs, total = {}, 0
+        for n_, t in src.items():
+            offs[n_] = total
+            total += (t.numel() * t.element_size() + 255) // 256 * 256
+        stage_h = torch.empty(total, dtype=torch.uint8).pin_memory()
+        stage_d = torch.empty(total, dtype=torch.uint8, device=dev)
+
+        def field_view(buf, n_):
+            t = src[n_]
+            nb = t.numel() * t.element_size()
+            return buf[offs[n_]:offs[n_] + nb].view(t.dtype).view(t.shape)
+
+        host_in = {n_: field_view(stage_h, n_) for n_ in src}
+        for n_, t in src.items():
+            host_in[n_].copy_(t)
+        dev_in = {n_: field_view(stage_d, n_) for n_ in src}
+        meta_bytes = offs["qkv"]
         rope = torch.empty(CTX, DIM, dtype=torch.float32, device=dev)
         nvb.rope_cache(rope, CTX, DIM, 1e6)
         q_dev = torch.empty(batch, QH, DIM, dtype=torch.bfloat16, device=dev)
-        h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+        qkv_bytes = src["qkv"].numel() * src["qkv"].element_size()
         d2h = out_h.numel() * out_h.element_size()
 
         # The step is pipelined over sequence chunks on three streams: chunk
@@ -397,6 +415,7 @@ def main():
             bounds = [(c * batch // nch, (c + 1) * batch // nch) for c in range(nch)]
         nch = len(bounds)
         e2e_sizes = [b - a for a, b in bounds]
+        h2d = total if nch == 1 else meta_bytes + qkv_bytes  # bytes copied per step
         h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
         chunk_cfg = []
         for s0, s1 in bounds:
@@ -410,12 +429,14 @@ def main():
         def e2e_step():
             h2d_s.wait_stream(stream)
             with torch.cuda.stream(h2d_s):
-                for n_, t in host_in.items():
-                    if n_ != "qkv":
-                        dev_in[n_].copy_(t, non_blocking=True)
-                for c, (s0, s1, *_r) in enumerate(chunk_cfg):
-                    dev_in["qkv"][s0:s1].copy_(qkv_h[s0:s1], non_blocking=True)
-                    ev_in[c].record(h2d_s)
+                if len(chunk_cfg) == 1:
+                    stage_d.copy_(stage_h, non_blocking=True)
+                    ev_in[0].record(h2d_s)
+                else:
+                    stage_d[:meta_bytes].copy_(stage_h[:meta_bytes], non_blocking=True)
+                    for c, (s0, s1, *_r) in enumerate(chunk_cfg):
+                        dev_in["qkv"][s0:s1].copy_(host_in["qkv"][s0:s1], non_blocking=True)
+                        ev_in[c].record(h2d_s)
             stream.wait_stream(d2h_s)
             for c, (s0, s1, sp, la_c, oa_c) in enumerate(chunk_cfg):
                 n = s1 - s0
