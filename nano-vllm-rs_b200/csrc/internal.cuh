@@ -69,7 +69,11 @@ int make_map_3d(const void* base, const uint64_t dims[3], const uint64_t strides
                 const uint32_t box[3], CUtensorMapSwizzle swizzle, const CUtensorMap** out);
 
 // Returns cudaErrorNotSupported when the tcgen05 path does not cover the shape.
+// launch_prefill picks the kernel: pairs of query tiles per work item
+// (prefill.cu) when a sequence can span more than one 128-row query tile,
+// else one tile per item (prefill_tile.cu).
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
+cudaError_t launch_prefill_tile(const PrefillArgs& a, cudaStream_t stream);
 
 // Native-form attention for head dimensions other than 128 (generic.cu).
 cudaError_t launch_generic_attention(const void* q, const void* k, const void* v, void* out, const int* positions,

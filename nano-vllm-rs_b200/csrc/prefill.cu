@@ -8,43 +8,46 @@
 // reference's: query i of a q_len-query group sees keys
 // [0, kv_len - q_len + i] (src/model.rs:1170-1188, smoke.cu:58).
 //
-// Work item: one 128-row query tile of one (sequence, kv head). Rows pack the
-// GQA group: row r is (query q0 + r / G, head h*G + r % G), so each K/V tile
-// serves every query head of the group. Per 128-key KV tile t:
+// Work item: a pair of adjacent 128-row query tiles A and B of one (sequence,
+// kv head). Rows pack the GQA group: row r of a tile is (query q0 + r / G,
+// head h*G + r % G), so each K/V tile serves every query head of the group,
+// and both tiles of the pair. Per 128-key KV tile j and tile x in {A, B}:
 //
-//   S_t = Q K_t^T   tcgen05.mma kind::f16, M=128 N=128 K=128 (8 x K16), A and B
-//                   from 128B-swizzled shared memory, D in TMEM (FP32)
-//   P_t = exp2(S_t * scale*log2e - m)   two softmax warpgroups, each thread
-//                   one row and one half (64 keys) of the tile; P written back
-//                   over S_t in TMEM as packed BF16
-//   O  += P_t V_t   tcgen05.mma M=128 N=128 K=128, A (P) read from TMEM, V an
-//                   MN-major B operand in shared memory, O in TMEM
+//   S_x = Q_x K_j^T   tcgen05.mma kind::f16, M=128 N=128 K=128 (8 x K16), A and
+//                     B from 128B-swizzled shared memory, D in TMEM (FP32)
+//   P_x = exp2(S_x * scale*log2e - m)   softmax warpgroup x, each thread one
+//                     row and all 128 keys; P written back over S_x in TMEM as
+//                     packed BF16
+//   O_x += P_x V_j    tcgen05.mma M=128 N=128 K=128, A (P) read from TMEM, V an
+//                     MN-major B operand in shared memory, O_x in TMEM
 //
-// S/P is triple-buffered in TMEM (columns 0, 128, 256; O at 384): S_{t+1} is
-// issued as soon as PV_{t-2} has released its buffer, so the tensor core
-// computes the next scores while the softmax works on the current ones and
-// the per-tile work of the tensor core (1024 cycles at M=N=K=128) overlaps the
-// softmax (~2,000 cycles a tile for the two warps of an SMSP, of which the
-// exponentials take ~1,100 on the 16-per-clock MUFU unit).
+// TMEM: S_A 0, S_B 128, O_A 256, O_B 384 (512 columns). S_x is single-buffered,
+// so each tile's chain is softmax -> PV -> next S -> softmax; the two tiles'
+// chains run out of phase on the tensor core (S_A, S_B, PV_A, PV_B), so one
+// softmax warpgroup's loads and max overlap the other's exponentials, and no
+// thread exchanges a row max with another. Sequences whose queries all fit
+// one tile (short chunks) go to the one-tile kernel in prefill_tile.cu, where
+// a pair would leave tile B empty.
 //
 // Roles (16 warps, one CTA per SM):
 //   warp 0      claims items (global counter, heaviest first), publishes each
-//               to the CTA through a two-slot ring, loads Q (two buffers) and
+//               to the CTA through a two-slot ring, loads Q_A and Q_B (one
+//               buffer each, reloaded when the tile's last S has read it) and
 //               the K tiles (two-stage ring) with TMA: 3-D maps over [tokens,
 //               kv_heads, 128], 64-element 128-byte-swizzled boxes; a 128-key
 //               tile never crosses a page since block_size is a multiple of 256
 //   warp 1      TMEM owner; one thread issues the S MMAs and their commits
 //   warp 2      V fixer and PV issuer: zeroes V rows that are not real keys
 //               (past kv_len or an invalid page) so P ~ 0 never meets a
-//               non-finite cache value, then one thread issues that tile's
-//               PV MMAs once P is in TMEM (two issuing threads: neither the
-//               S nor the PV stream waits behind the other's barriers)
+//               non-finite cache value, then one thread issues the tile's PV
+//               MMAs once P is in TMEM (two issuing threads: neither the S
+//               nor the PV stream waits behind the other's barriers)
 //   warp 3      loads the V tiles (two-stage ring)
-//   warps 4-7   softmax of keys 0-63 of each tile; warps 8-11 keys 64-127. The
-//               two halves of a row agree on its max through shared memory and
-//               a per-quadrant mbarrier (no bar.sync: every wait is bounded)
-//   warps 12-15 epilogue: O / l -> BF16 rows and the LSE, from row statistics
-//               handed over in shared memory; frees O for the next item
+//   warps 4-7   softmax of tile A; warps 8-11 softmax of tile B (200 registers
+//               a thread through setmaxnreg: a row's 128 scores stay in
+//               registers)
+//   warps 12-15 epilogue: O_x / l -> BF16 rows and the LSE, from row statistics
+//               handed over in shared memory; frees O_x for its next tile
 //
 // The softmax keeps the running max it scales by unless a row's max grows by
 // more than 2^8 (lazy rescale: P stays <= 256, exact after the final divide),
@@ -59,43 +62,47 @@
 // TMEM and exits.
 #include <mutex>
 
-#include "internal.cuh"
+#include "prefill_common.cuh"
 
 namespace nvb {
 
 namespace prefill_detail {
 
-constexpr int kRows = 128;                   // query rows per item (TMEM lanes)
+using namespace prefill_common;
+
+constexpr int kRows = 128;                   // query rows per Q tile (TMEM lanes)
 constexpr int kKeys = 128;                   // keys per KV tile
 constexpr int kHalf = 128 * 128;             // 128 rows x 64 BF16 (one 128-byte swizzle column)
 constexpr int kQBytes = 2 * kHalf;           // Q tile 128 x 128 BF16
 constexpr int kKVBytes = 2 * kHalf;          // K or V tile 128 x 128 BF16
-constexpr int kQStages = 2, kKStages = 2, kVStages = 2;
-constexpr int kSBufs = 3;                    // S/P buffers in TMEM
+constexpr int kQStages = 2, kKStages = 2, kVStages = 2;  // Q: tiles A and B of the item
 constexpr int kThreads = 512;
 constexpr int kTmemCols = 512;
-constexpr int kOCol = 384;
+constexpr int kSCol = 0, kOCol = 256;        // S/P of tile x at kSCol + 128 x, O at kOCol + 128 x
 constexpr float kLn2 = 0.693147180559945309f;
 constexpr float kRescaleLog2 = 8.0f;         // lazy rescale threshold (P <= 2^8)
+// Register split after set-up (launch: 512 threads x 128 a thread): the two
+// softmax warpgroups hold a tile row's 128 scores; the producer/MMA and
+// epilogue warpgroups run on the rest.
+constexpr int kLaunchRegs = 128, kSoftmaxRegs = 200, kOtherRegs = 56;
+static_assert(2 * 128 * kSoftmaxRegs + 2 * 128 * kOtherRegs == kThreads * kLaunchRegs, "register split");
 
+// mbarriers, [2] = per Q tile (A, B) or per ring stage
 enum Bar {
-  kQFull = 0, kQFree = 2, kKFull = 4, kKEmpty = 6, kVFull = 8, kPVDrain = 10, kVEmpty = 12,  // [2]
-  kSFull = 14, kPVDone = 17, kPFull = 20,                                                  // [3]: per S buffer
-  kODone = 23, kOFree = 24, kStatsFull = 25, kStatsFree = 26,
-  kXchg = 27,                                                                              // [4]: per TMEM quadrant
-  kItemFull = 31, kItemEmpty = 33,                                                         // [2]
-  kDrain = 35, kNumBars = 36
+  kQFull = 0, kQFree = 2, kKFull = 4, kKEmpty = 6, kVFull = 8, kVEmpty = 10,
+  kSFull = 12, kPFull = 14, kPVDone = 16, kODone = 18, kOFree = 20, kStatsFull = 22, kStatsFree = 24,
+  kItemFull = 26, kItemEmpty = 28,
+  kDrain = 30, kPVDrain = 31, kNumBars = 32
 };
-// Readers of each published item: V producer, MMA issuer, V fixer (one
+// Readers of each published item: V producer, S issuer, V fixer (one
 // arrival each) and the 8 softmax + 4 epilogue warps (one per warp).
 constexpr int kItemReaders = 15;
 constexpr int kTmemSlotOff = kNumBars * 8;
 constexpr int kItemOff = 320;                               // Item [2] (the published-item ring)
 constexpr int kItemBytes = 64;
-constexpr int kStatsOff = 512;                              // float2 [128]: row max used, row sum
-constexpr int kXOff = kStatsOff + kRows * 8;                // float [2 slots][2 halves][128]
+constexpr int kStatsOff = 512;                              // float2 [2][128]: row max used, row sum
 constexpr int kMaxSorted = 1024;                            // batches up to this size are claimed by work
-constexpr int kOrderOff = kXOff + 2 * 2 * kRows * 4;        // int [kMaxSorted]: sequences, heaviest first
+constexpr int kOrderOff = kStatsOff + 2 * kRows * 8;        // int [kMaxSorted]: sequences, heaviest first
 constexpr int kWorkOff = kOrderOff + kMaxSorted * 4;        // float [kMaxSorted]: each sequence's work
 constexpr int kHeadBytes = kWorkOff + kMaxSorted * 4;
 constexpr int kQOff = 0;                                    // offsets from the 1 KB aligned tile base
@@ -116,186 +123,54 @@ struct PrefillParams {
   int batch, max_q, qh, kvh, group, qt, rows_used, block_size, table_stride, num_blocks;
   float scale_log2;
   int* sched;  // {next item to claim, CTAs finished}: zero at launch, reset by the last CTA
-  FastDiv fd_nqt, fd_kvh, fd_qt, fd_bs;  // by n_qtiles, kvh, qt, block_size
+  int n_pairs;  // query-tile pairs of the longest sequence
+  FastDiv fd_npair, fd_kvh, fd_qt, fd_bs;  // by n_pairs, kvh, qt, block_size
 };
 
-// ------------------------------------------------------------- tcgen05 PTX
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 format: start
-// address >> 4 in bits 0-13, leading byte offset >> 4 in 16-29, stride byte
-// offset >> 4 in 32-45, version 1 in bits 46-47, layout type 2 in 61-63).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
-         (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) | (uint64_t(2) << 61);
-}
-
-// Instruction descriptors, kind::f16: FP32 accumulator, BF16 A and B, A
-// K-major, M = 128, N = 128. S = Q K^T: B K-major (keys). O += P V: B
-// MN-major (head dims contiguous).
-constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 4) << 24) | ((128u >> 3) << 17);
-constexpr uint32_t kIdescS = kIdescBase;
-constexpr uint32_t kIdescPV = kIdescBase | (1u << 16);
-
-// D (+)= A B with A and B from shared memory (umma_ss) or A from TMEM
-// (umma_ts); each shared-memory descriptor is passed as its (low, high)
-// words. The issuer builds every descriptor once and moves between
-// stages and K16 steps by adding (byte offset >> 4) to the low word: the start
-// address field is bits 0-13 and shared addresses stay below 2^18, so the add
-// never carries out of it. This keeps the one issuing thread, which shares
-// its SMSP with two softmax warps, at a few instructions per MMA.
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo, uint32_t b_hi,
-                                        uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\tsetp.ne.b32 p, %6, 0;\n\t"
-      "mov.b64 da, {%1, %2};\n\tmov.b64 db, {%3, %4};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(acc)
-      : "memory");
-}
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
-                                        uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\tsetp.ne.b32 p, %5, 0;\n\t"
-      "mov.b64 db, {%2, %3};\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(acc)
-      : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-
-// Packed FP32 pairs (Blackwell f32x2 ALU forms): d = a * b + c, d = a + b.
-__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
-                                     float c1) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
-}
-
-__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// 2^x for a pair of inputs on the FMA pipe (x <= 128), for a share of the
-// softmax beside the 16-per-clock MUFU unit. Range reduction x = n + f with
-// n the nearest integer (1.5 * 2^23 rounding trick, |f| <= 1/2), a degree-4
-// polynomial for 2^f fitted to minimise relative error on [-1/2, 1/2] (this
-// file's own fit; max relative error 2.7e-6 in FP32), then n added to the
-// exponent field with one integer multiply-add. Inputs are clamped at -125,
-// so a masked key (-inf) gives 2^-125 rather than 0: ~1e-38 of a value that
-// the caller's V zeroing or row statistics make irrelevant.
-__device__ __forceinline__ void exp2_fma_pair(float& a, float& b) {
-  const float xa = fmaxf(a, -125.0f), xb = fmaxf(b, -125.0f);
-  float ta, tb, na, nb, fa, fb, pa, pb;
-  add2(ta, tb, xa, xb, 12582912.0f, 12582912.0f);
-  add2(na, nb, ta, tb, -12582912.0f, -12582912.0f);
-  fma2(fa, fb, na, nb, -1.0f, -1.0f, xa, xb);  // f = x - round(x)
-  fma2(pa, pb, 0.009570096619427204f, 0.009570096619427204f, fa, fb, 0.05591785907745361f, 0.05591785907745361f);
-  fma2(pa, pb, pa, pb, fa, fb, 0.240247443318367f, 0.240247443318367f);
-  fma2(pa, pb, pa, pb, fa, fb, 0.6931217908859253f, 0.6931217908859253f);
-  fma2(pa, pb, pa, pb, fa, fb, 0.9999992847442627f, 0.9999992847442627f);
-  a = __int_as_float(__float_as_int(ta) * 8388608 + __float_as_int(pa));  // exponent += round(x)
-  b = __int_as_float(__float_as_int(tb) * 8388608 + __float_as_int(pb));
-}
-
-#define NVB_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), \
-                  "=r"(r[i + 6]), "=r"(r[i + 7])
-#define NVB_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), "r"(r[i + 5]), \
-                  "r"(r[i + 6]), "r"(r[i + 7])
-
-// 32 consecutive FP32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : NVB_R8(0), NVB_R8(8), NVB_R8(16), NVB_R8(24)
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      NVB_W8(0), NVB_W8(8), NVB_W8(16), NVB_W8(24)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      NVB_W8(0), NVB_W8(8)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-__device__ __forceinline__ void st_shared_zero16(uint32_t addr) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0) : "memory");
-}
-
-__device__ __forceinline__ bool page_ok(int page, int num_blocks) { return page >= 0 && page < num_blocks; }
-
-
-// Every lane of the warp waits; the warp continues only if all of them saw
-// the phase complete, so a timeout never splits the warp before the
-// .sync.aligned TMEM instructions that follow.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, kErrPrefillWait));
-}
-
-// One 128-row query tile of one (sequence, kv head): the work item of the
-// persistent loop. Virtual items are grouped by (sequence, kv head), longest
-// causal tile first within a group, so the CTAs running at one time share a
-// few groups' K/V in L2; the sequences come heaviest first (ranked at kernel
-// start for batches up to kMaxSorted) and CTAs claim items from a global
-// counter (dynamic load balancing), so the last claims are small ones.
+// Two adjacent 128-row query tiles (A = q-tile 2k, B = q-tile 2k + 1) of one
+// (sequence, kv head): the work item of the persistent loop. A and B share
+// every K/V tile; each has its own S/P and O in TMEM and its own softmax
+// warpgroup. Virtual items are grouped by (sequence, kv head), longest pair
+// first within a group, so the CTAs running at one time share a few groups'
+// K/V in L2; the sequences come heaviest first (ranked at kernel start for
+// batches up to kMaxSorted) and CTAs claim items from a global counter
+// (dynamic load balancing), so the last claims are small ones.
 struct Item {
-  int b, h, q_begin, q0, kv_len, prefix;
-  int qx;       // queries in the tile
-  int key_end;  // keys its last query sees
-  int n;        // KV tiles it visits
-  int full;     // leading KV tiles that every row sees whole
+  int b, h, q_begin, kv_len, prefix;
+  int q0[2];       // first query of tile A / B within the sequence
+  int qx[2];       // queries in the tile (0: tile B is past the sequence)
+  int n[2];        // KV tiles the tile visits (0 for an empty tile)
+  int full[2];     // leading KV tiles every row of the tile sees whole
+  int key_end[2];  // keys the tile's last query sees
 };
 static_assert(sizeof(Item) <= kItemBytes, "item ring slot too small");
+
+__device__ __forceinline__ int item_tiles(const Item& it) { return max(it.n[0], it.n[1]); }
 
 // `order` (or null): sequence of each rank, heaviest first.
 __device__ __forceinline__ Item make_item(const PrefillParams& p, const int* order, int v) {
   Item it;
-  const int group = p.fd_nqt.div(v);
-  const int tile = p.n_qtiles - 1 - (v - group * p.n_qtiles);
+  const int group = p.fd_npair.div(v);
+  const int pair = p.n_pairs - 1 - (v - group * p.n_pairs);
   const int rank = p.fd_kvh.div(group);
   it.b = order ? order[rank] : rank;
   it.h = group - rank * p.kvh;
   it.q_begin = p.cu_q[it.b];
   const int q_len = p.cu_q[it.b + 1] - it.q_begin;
-  it.q0 = tile * p.qt;
-  it.qx = max(0, min(p.qt, q_len - it.q0));
-  it.kv_len = it.qx > 0 ? p.kv_lens[it.b] : 0;
+  it.kv_len = p.kv_lens[it.b];
   it.prefix = it.kv_len - q_len;
   // A context longer than the page table, or shorter than its query group,
   // is invalid input: such rows get zero output (as decode does).
-  const bool seq_ok = it.qx > 0 && it.prefix >= 0 && (long long)it.kv_len <= (long long)p.table_stride * p.block_size;
-  it.key_end = seq_ok ? min(it.kv_len, it.prefix + it.q0 + it.qx) : 0;
-  it.n = (it.key_end + kKeys - 1) / kKeys;
-  it.full = seq_ok ? min(it.kv_len, it.prefix + it.q0 + 1) / kKeys : 0;
+  const bool ctx_ok = it.prefix >= 0 && (long long)it.kv_len <= (long long)p.table_stride * p.block_size;
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    it.q0[x] = (2 * pair + x) * p.qt;
+    it.qx[x] = max(0, min(p.qt, q_len - it.q0[x]));
+    const bool ok = ctx_ok && it.qx[x] > 0;
+    it.key_end[x] = ok ? min(it.kv_len, it.prefix + it.q0[x] + it.qx[x]) : 0;
+    it.n[x] = (it.key_end[x] + kKeys - 1) / kKeys;
+    it.full[x] = ok ? min(it.kv_len, it.prefix + it.q0[x] + 1) / kKeys : 0;
+  }
   return it;
 }
 
@@ -320,6 +195,160 @@ __device__ __forceinline__ bool take_item(uint64_t* bars, const Item* ring, int 
   return it.b >= 0;
 }
 
+// exp2(s * sl2 + nm) for keys [C0, C0 + 32) of a row -> 16 packed BF16 pairs;
+// row-sum partials accumulate in `sum`. One pair in eight runs on the FMA pipe.
+template <int C0>
+__device__ __forceinline__ void exp32(const float (&s)[128], float sl2, float nm, uint32_t (&pk)[16],
+                                      float (&sum)[8]) {
+#pragma unroll
+  for (int c = C0; c < C0 + 32; c += 2) {
+    float e0 = s[c], e1 = s[c + 1];
+    fma2(e0, e1, e0, e1, sl2, sl2, nm, nm);
+    if ((c & 15) == 14) {
+      exp2_fma_pair(e0, e1);
+    } else {
+      e0 = fast_exp2(e0);
+      e1 = fast_exp2(e1);
+    }
+    const int k = (c >> 1) & 3;  // four independent accumulator pairs
+    add2(sum[2 * k], sum[2 * k + 1], sum[2 * k], sum[2 * k + 1], e0, e1);
+    pk[(c - C0) >> 1] = pack_bf16x2(e0, e1);
+  }
+}
+
+// Softmax of Q tile x (warps 4-7: A, 8-11: B): one thread per row, all 128
+// keys of each KV tile, so no other thread takes part in a row's max. P goes
+// back over the first 64 columns of S_x as packed BF16. The running max only
+// moves when a row's max grows by more than 2^8 (lazy rescale); O_x is then
+// rescaled here, and is quiescent: S_x of this tile was issued after PV_x of
+// the previous one completed, and PV_x of this tile waits for this P.
+__device__ __forceinline__ void softmax_role(const PrefillParams& p, uint64_t* bars, const Item* ring, float2* stats,
+                                             uint32_t tmem, int warp, int lane) {
+  const int x = (warp - 4) >> 2;
+  const int quad = warp & 3;
+  const int r = quad * 32 + lane;  // TMEM lane = packed row
+  const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
+  const uint32_t scol = lane_base + kSCol + x * kKeys, ocol = lane_base + kOCol + x * kKeys;
+  const int rq = r / p.group;
+  const float sl2 = p.scale_log2;
+  int t = 0, ix = 0;  // tiles and items of this Q tile
+  bool alive = true;
+  Item it;
+  for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
+    // this tile's fields (selects: a run-time index would put the item in local memory)
+    const int n = x ? it.n[1] : it.n[0];
+    if (n == 0) continue;
+    const int full = x ? it.full[1] : it.full[0];
+    const int qx = x ? it.qx[1] : it.qx[0], q0 = x ? it.q0[1] : it.q0[0];
+    const int key_end = x ? it.key_end[1] : it.key_end[0];
+    const int* table = p.block_table + (long long)it.b * p.table_stride;
+    const bool valid_row = r < p.rows_used && rq < qx;
+    const int limit = valid_row ? it.prefix + q0 + rq : key_end - 1;  // last visible key
+    float m_used = -INFINITY, l = 0.0f;  // running max the probabilities are scaled by
+    for (int j = 0; j < n; ++j, ++t) {
+      const int key0 = j * kKeys;
+      const bool ok = page_ok(table[p.fd_bs.div(key0)], p.num_blocks);
+      if (!warp_wait(&bars[kSFull + x], t & 1)) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      float s[128];
+      {
+        uint32_t a0[32], a1[32], a2[32], a3[32];
+        tmem_ld32(scol, a0);
+        tmem_ld32(scol + 32, a1);
+        tmem_ld32(scol + 64, a2);
+        tmem_ld32(scol + 96, a3);
+        tmem_ld_wait();
+        reg_fence(a0);
+        reg_fence(a1);
+        reg_fence(a2);
+        reg_fence(a3);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          s[c] = __uint_as_float(a0[c]);
+          s[32 + c] = __uint_as_float(a1[c]);
+          s[64 + c] = __uint_as_float(a2[c]);
+          s[96 + c] = __uint_as_float(a3[c]);
+        }
+      }
+      if (j >= full || !ok) {
+        const int lim = ok ? min(limit, it.kv_len - 1) - key0 : -1;
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c > lim) s[c] = -INFINITY;
+      }
+      float mx8[8];
+#pragma unroll
+      for (int i8 = 0; i8 < 8; ++i8) mx8[i8] = s[i8];
+#pragma unroll
+      for (int c = 8; c < 120; c += 16) {
+#pragma unroll
+        for (int i8 = 0; i8 < 8; ++i8) mx8[i8] = max3(mx8[i8], s[c + i8], s[c + 8 + i8]);
+      }
+#pragma unroll
+      for (int i8 = 0; i8 < 8; ++i8) mx8[i8] = fmaxf(mx8[i8], s[120 + i8]);
+      const float m_tile =
+          max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])) * sl2;
+      // Rescale only when the row max grew by more than 2^8 (or on the first
+      // finite max); otherwise keep scaling by the stale max.
+      float alpha = 1.0f;
+      if (m_tile > m_used + kRescaleLog2) {
+        alpha = fast_exp2(m_used - m_tile);  // 0 when m_used = -inf
+        m_used = m_tile;
+      }
+      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        // PV_x of the previous tile completed before S_x of this one was
+        // issued; the wait (already satisfied) orders its O writes here.
+        if (!warp_wait(&bars[kPVDone + x], (t - 1) & 1)) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {
+          uint32_t o[32];
+          tmem_ld32(ocol + h * 32, o);
+          tmem_ld_wait();
+          reg_fence(o);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+          tmem_st32(ocol + h * 32, o);
+        }
+      }
+      const float nm = m_used == -INFINITY ? 0.0f : -m_used;
+      float sum[8];
+#pragma unroll
+      for (int i8 = 0; i8 < 8; ++i8) sum[i8] = 0.0f;
+      {
+        // keys [32 g, +32) -> packed columns [16 g, +16) of S_x
+        uint32_t pk[16];
+        exp32<0>(s, sl2, nm, pk, sum);
+        tmem_st16(scol, pk);
+        exp32<32>(s, sl2, nm, pk, sum);
+        tmem_st16(scol + 16, pk);
+        exp32<64>(s, sl2, nm, pk, sum);
+        tmem_st16(scol + 32, pk);
+        exp32<96>(s, sl2, nm, pk, sum);
+        tmem_st16(scol + 48, pk);
+      }
+      l = l * alpha + (((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7])));
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kPFull + x]);
+    }
+    if (!alive) break;
+    // (max used, row sum) to the epilogue through a one-item slot per tile
+    if (ix > 0 && !warp_wait(&bars[kStatsFree + x], (ix - 1) & 1)) break;
+    // no finite score seen: the sum holds only clamped-exponent residue
+    stats[x * kRows + r] = make_float2(m_used, m_used == -INFINITY ? 0.0f : l);
+    mbar_arrive(&bars[kStatsFull + x]);
+    ++ix;
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap qmap,
                    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
@@ -329,14 +358,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sbase = (raw_addr + 1023u) & ~1023u;
   unsigned char* tiles = smem_raw + (sbase - raw_addr);
   unsigned char* head = tiles + kTileBytes;
-  const int n_items = p.n_qtiles * p.batch * p.kvh;
+  const int n_items = p.n_pairs * p.batch * p.kvh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(head);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(head + kTmemSlotOff);
   Item* ring = reinterpret_cast<Item*>(head + kItemOff);
   float2* stats = reinterpret_cast<float2*>(head + kStatsOff);
-  float* xch = reinterpret_cast<float*>(head + kXOff);
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
@@ -345,24 +373,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars[kKFull + s], 1);
       mbar_init(&bars[kKEmpty + s], 1);
       mbar_init(&bars[kVFull + s], 1);
-      mbar_init(&bars[kPVDrain + s], 1);
       mbar_init(&bars[kVEmpty + s], 1);
+      mbar_init(&bars[kSFull + s], 1);
+      mbar_init(&bars[kPFull + s], 4);
+      mbar_init(&bars[kPVDone + s], 1);
+      mbar_init(&bars[kODone + s], 1);
+      mbar_init(&bars[kOFree + s], 4);
+      mbar_init(&bars[kStatsFull + s], kRows);
+      mbar_init(&bars[kStatsFree + s], kRows);
       mbar_init(&bars[kItemFull + s], 1);
       mbar_init(&bars[kItemEmpty + s], kItemReaders);
     }
-#pragma unroll
-    for (int b = 0; b < kSBufs; ++b) {
-      mbar_init(&bars[kSFull + b], 1);
-      mbar_init(&bars[kPVDone + b], 1);
-      mbar_init(&bars[kPFull + b], 8);
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) mbar_init(&bars[kXchg + q], 64);
-    mbar_init(&bars[kODone], 1);
-    mbar_init(&bars[kOFree], 4);
-    mbar_init(&bars[kStatsFull], kRows);
-    mbar_init(&bars[kStatsFree], kRows);
     mbar_init(&bars[kDrain], 1);
+    mbar_init(&bars[kPVDrain], 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -409,431 +432,322 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------- scheduler, Q and K producer
-    if (lane == 0) {
-      tma_prefetch_desc(&qmap);
-      tma_prefetch_desc(&kmap);
-      tma_prefetch_desc(&vmap);
-      int gt = 0, ix = 0, k_issued = 0;
-      bool alive = true;
-      for (int i = 0; alive; ++i) {
-        // claim the next item that has queries
-        int v;
-        Item it;
-        do {
-          v = atomicAdd(p.sched, 1);
-          if (v >= n_items) break;
-          it = make_item(p, order, v);
-          if (it.qx == 0) {
-            // Tiles past the sequence's queries come first in their group:
-            // move the counter to the group's last (non-empty) tile if nobody
-            // has claimed past this one yet.
-            const int q_len = p.cu_q[it.b + 1] - it.q_begin;
-            const int tiles = q_len > 0 ? p.fd_qt.div(q_len + p.qt - 1) : 0;
-            const int group_end = (p.fd_nqt.div(v) + 1) * p.n_qtiles;
-            atomicCAS(p.sched, v + 1, group_end - tiles);
-          }
-        } while (it.qx == 0);
-        const bool end = v >= n_items;
-        if (end) it.b = -1;
-        if (i >= 2 && !mbar_wait(&bars[kItemEmpty + (i & 1)], ((i >> 1) + 1) & 1, kErrPrefillWait)) break;
-        ring[i & 1] = it;
-        mbar_arrive(&bars[kItemFull + (i & 1)]);
-        if (end) break;
-        if (it.n == 0) continue;  // rows without keys: only the epilogue acts
-        const int qs = ix & 1;
-        // Q buffer qs is free once the last S MMA of item ix-2 completed.
-        if (ix >= 2 && !mbar_wait(&bars[kQFree + qs], ((ix >> 1) + 1) & 1, kErrPrefillWait)) break;
-        mbar_arrive_expect_tx(&bars[kQFull + qs], 2u * 128u * uint32_t(p.rows_used));
-        {
-          const int qy = it.h * p.group, qz = it.q_begin + it.q0;
-          unsigned char* qdst = tiles + kQOff + qs * kQBytes;
-          tma_load_3d(qdst, &qmap, &bars[kQFull + qs], 0, qy, qz);
-          tma_load_3d(qdst + kHalf, &qmap, &bars[kQFull + qs], 64, qy, qz);
-        }
-        ++ix;
-        const int* table = p.block_table + (long long)it.b * p.table_stride;
-        for (int j = 0; j < it.n; ++j) {
-          const int g = gt + j, st = g & 1;
-          const int key0 = j * kKeys;
-          const int logical = p.fd_bs.div(key0);
-          const int page = table[logical];
-          const bool ok = page_ok(page, p.num_blocks);
-          const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
-          if (g >= kKStages && !mbar_wait(&bars[kKEmpty + st], ((g >> 1) + 1) & 1, kErrPrefillWait)) {
-            alive = false;
-            break;
-          }
-          unsigned char* kdst = tiles + kKOff + st * kKVBytes;
-          if (ok) {
-            mbar_arrive_expect_tx(&bars[kKFull + st], kKVBytes);
-            tma_load_3d(kdst, &kmap, &bars[kKFull + st], 0, it.h, trow);
-            tma_load_3d(kdst + kHalf, &kmap, &bars[kKFull + st], 64, it.h, trow);
-          } else {
-            mbar_arrive(&bars[kKFull + st]);
-          }
-          k_issued = g + 1;
-        }
-        gt += it.n;
-      }
-      // Drain: every copy this thread issued has landed before the CTA exits
-      // (already true on the normal path; bounded on an error path).
-#pragma unroll
-      for (int s = 0; s < 2; ++s) {
-        if (k_issued > s) mbar_wait(&bars[kKFull + s], ((k_issued - 1 - s) >> 1) & 1, kErrPrefillWait);
-        if (ix > s) mbar_wait(&bars[kQFull + s], ((ix - 1 - s) >> 1) & 1, kErrPrefillWait);
-      }
-    }
-  } else if (warp == 3) {
-    // ------------------------------------------------------- V producer
-    if (lane == 0) {
-      tma_prefetch_desc(&vmap);
-      int gt = 0, v_issued = 0;
-      bool alive = true;
-      Item it;
-      for (int i = 0; alive && take_item(bars, ring, i, false, it); ++i) {
-        if (it.n == 0) continue;
-        const int* table = p.block_table + (long long)it.b * p.table_stride;
-        for (int j = 0; j < it.n; ++j) {
-          const int g = gt + j, st = g & 1;
-          const int key0 = j * kKeys;
-          const int logical = p.fd_bs.div(key0);
-          const int page = table[logical];
-          const bool ok = page_ok(page, p.num_blocks);
-          const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
-          if (g >= kVStages && !mbar_wait(&bars[kVEmpty + st], ((g >> 1) + 1) & 1, kErrPrefillWait)) {
-            alive = false;
-            break;
-          }
-          unsigned char* vdst = tiles + kVOff + st * kKVBytes;
-          if (ok) {
-            mbar_arrive_expect_tx(&bars[kVFull + st], kKVBytes);
-            tma_load_3d(vdst, &vmap, &bars[kVFull + st], 0, it.h, trow);
-            tma_load_3d(vdst + kHalf, &vmap, &bars[kVFull + st], 64, it.h, trow);
-          } else {
-            mbar_arrive(&bars[kVFull + st]);
-          }
-          v_issued = g + 1;
-        }
-        gt += it.n;
-      }
-#pragma unroll
-      for (int s = 0; s < 2; ++s)
-        if (v_issued > s) mbar_wait(&bars[kVFull + s], ((v_issued - 1 - s) >> 1) & 1, kErrPrefillWait);
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      int gt = 0, ix = 0;  // tiles and items (with keys) so far
-      bool alive = true;
-      // Descriptors of stage 0 of Q, K and V; stages are 2048 16-byte units apart.
-      const uint64_t qd = sw128_desc(sbase + kQOff, 16, 1024), kd = sw128_desc(sbase + kKOff, 16, 1024);
-      const uint32_t q_lo = uint32_t(qd), q_hi = uint32_t(qd >> 32), k_lo = uint32_t(kd), k_hi = uint32_t(kd >> 32);
-      static_assert(kQBytes == kKVBytes && kKVBytes >> 4 == 2048, "stage stride in descriptor units");
-      Item it;
-      for (int i = 0; alive && take_item(bars, ring, i, false, it); ++i) {
-        if (it.n == 0) continue;
-        const int qs = ix & 1;
-        for (int j = 0; j < it.n && alive; ++j) {
-          const int t = gt + j, ks = t & 1, buf = t % kSBufs;
-          alive = mbar_wait(&bars[kKFull + ks], (t >> 1) & 1, kErrPrefillWait);
-          if (alive && j == 0) alive = mbar_wait(&bars[kQFull + qs], (ix >> 1) & 1, kErrPrefillWait);
-          // buffer `buf` last held P_{t-3}: PV_{t-3} must have read it
-          if (alive && t >= kSBufs)
-            alive = mbar_wait(&bars[kPVDone + buf], ((t - kSBufs) / kSBufs) & 1, kErrPrefillWait);
-          if (!alive) break;
-          tc_fence_after();
-          const uint32_t qa = q_lo + uint32_t(qs) * 2048u, kb = k_lo + uint32_t(ks) * 2048u, sd = tmem + buf * kKeys;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = uint32_t((kk >> 2) * kHalf + (kk & 3) * 32) >> 4;
-            umma_ss(sd, qa + off, q_hi, kb + off, k_hi, kIdescS, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&bars[kSFull + buf]);
-          umma_commit(&bars[kKEmpty + ks]);
-          if (j == it.n - 1) umma_commit(&bars[kQFree + qs]);
-        }
-        if (!alive) break;
-        ++ix;
-        gt += it.n;
-      }
-      // every MMA issued by this thread completes before TMEM is freed
-      umma_commit(&bars[kDrain]);
-      mbar_wait(&bars[kDrain], 0, kErrPrefillWait);
-    }
-  } else if (warp == 2) {
-    // ------------------------------------------- V fixer and PV issuer
-    // Fixes V_t, then lane 0 issues O += P_t V_t (the S MMAs come from warp
-    // 1: two issuing threads, so neither stream waits behind the other's
-    // barriers). The item's first PV also waits for the epilogue's read of the
-    // previous item's O.
-    int gt = 0, ix = 0;
-    bool alive = true;
-    const uint64_t vd = sw128_desc(sbase + kVOff, kHalf, 1024);
-    const uint32_t v_lo = uint32_t(vd), v_hi = uint32_t(vd >> 32);
-    Item it;
-    for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
-      if (it.n == 0) continue;
-      const int* table = p.block_table + (long long)it.b * p.table_stride;
-      for (int j = 0; j < it.n; ++j) {
-        const int g = gt + j, st = g & 1;
-        const int key0 = j * kKeys;
-        const bool ok = page_ok(table[p.fd_bs.div(key0)], p.num_blocks);
-        const int real = ok ? min(kKeys, it.kv_len - key0) : 0;
-        if (!warp_wait(&bars[kVFull + st], (g >> 1) & 1)) {
-          alive = false;
-          break;
-        }
-        if (real < kKeys) {
-          const uint32_t vbase = sbase + kVOff + st * kKVBytes;
-          for (int e = lane; e < (kKeys - real) * 16; e += 32) {
-            const int row = real + (e >> 4), c = e & 15;
-            st_shared_zero16(vbase + (c >> 3) * kHalf + row * 128 + (c & 7) * 16);
-          }
-          fence_proxy_async_smem();
-        }
-        __syncwarp();
-        bool ok_pv = true;
-        if (lane == 0) {
-          const int buf = g % kSBufs;
-          if (j == 0 && ix > 0) ok_pv = mbar_wait(&bars[kOFree], (ix - 1) & 1, kErrPrefillWait);
-          if (ok_pv) ok_pv = mbar_wait(&bars[kPFull + buf], (g / kSBufs) & 1, kErrPrefillWait);
-          if (ok_pv) {
-            tc_fence_after();
-            const uint32_t vb = v_lo + uint32_t(st) * 2048u, pa = tmem + buf * kKeys;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              // P: 16 keys = 8 packed columns; V: 16 keys = 2048 bytes of rows
-              umma_ts(tmem + kOCol, pa + kk * 8, vb + kk * 128, v_hi, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-            }
-            umma_commit(&bars[kPVDone + buf]);
-            umma_commit(&bars[kVEmpty + st]);
-            if (j == it.n - 1) umma_commit(&bars[kODone]);
-          }
-        }
-        if (!__shfl_sync(0xffffffffu, ok_pv, 0)) {
-          alive = false;
-          break;
-        }
-      }
-      ++ix;
-      gt += it.n;
-    }
-    if (lane == 0) {
-      // every PV MMA completes before TMEM is freed
-      umma_commit(&bars[kPVDrain]);
-      mbar_wait(&bars[kPVDrain], 0, kErrPrefillWait);
-    }
-  } else if (warp < 12) {
-    // ---------------------------------------------------------- softmax
-    const int hf = (warp - 4) >> 2;  // which 64 keys of each tile
-    const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // TMEM lane = packed row
-    const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
-    const int rq = r / p.group;
-    const float sl2 = p.scale_log2;
-    int t = 0, ix = 0, xc = 0;  // tiles, items with keys, max exchanges
-    bool alive = true;
-    // Exchange one value per row with the other half (same TMEM quadrant).
-    auto exchange = [&](float mine, float& other) -> bool {
-      float* slot = xch + (xc & 1) * 2 * kRows;
-      slot[hf * kRows + r] = mine;
-      mbar_arrive(&bars[kXchg + quad]);
-      if (!warp_wait(&bars[kXchg + quad], xc & 1)) return false;
-      other = slot[(1 - hf) * kRows + r];
-      ++xc;
-      return true;
-    };
-    Item it;
-    for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
-      if (it.n == 0) continue;
-      const int* table = p.block_table + (long long)it.b * p.table_stride;
-      const bool valid_row = r < p.rows_used && rq < it.qx;
-      const int limit = valid_row ? it.prefix + it.q0 + rq : it.key_end - 1;  // last visible key
-      float m_used = -INFINITY, l = 0.0f;  // running max the probabilities are scaled by
-      for (int j = 0; j < it.n; ++j, ++t) {
-        const int buf = t % kSBufs;
-        const int key0 = j * kKeys;
-        const bool ok = page_ok(table[p.fd_bs.div(key0)], p.num_blocks);
-        if (!warp_wait(&bars[kSFull + buf], (t / kSBufs) & 1)) {
-          alive = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t scol = lane_base + buf * kKeys;
-        float s[64];
-        {
-          uint32_t a0[32], a1[32];
-          tmem_ld32(scol + hf * 64, a0);
-          tmem_ld32(scol + hf * 64 + 32, a1);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            s[c] = __uint_as_float(a0[c]);
-            s[32 + c] = __uint_as_float(a1[c]);
-          }
-        }
-        if (j >= it.full || !ok) {
-          const int lim = (ok ? min(limit, it.kv_len - 1) - key0 : -1) - hf * 64;
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (c > lim) s[c] = -INFINITY;
-        }
-        float mx8[8];
-#pragma unroll
-        for (int i8 = 0; i8 < 8; ++i8) mx8[i8] = s[i8];
-#pragma unroll
-        for (int c = 8; c < 56; c += 16) {
-#pragma unroll
-          for (int i8 = 0; i8 < 8; ++i8) mx8[i8] = max3(mx8[i8], s[c + i8], s[c + 8 + i8]);
-        }
-#pragma unroll
-        for (int i8 = 0; i8 < 8; ++i8) mx8[i8] = fmaxf(mx8[i8], s[56 + i8]);
-        const float pm = max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
-        // The other half may overwrite S columns this half has read (its P
-        // store) once both have arrived.
-        tc_fence_before();
-        float om;
-        if (!exchange(pm, om)) {
-          alive = false;
-          break;
-        }
-        tc_fence_after();
-        const float m_tile = fmaxf(pm, om) * sl2;
-        // Rescale only when the row max grew by more than 2^8 (or on the
-        // first finite max); otherwise keep scaling by the stale max. Both
-        // halves see the same values, so they decide alike.
-        float alpha = 1.0f;
-        if (m_tile > m_used + kRescaleLog2) {
-          alpha = fast_exp2(m_used - m_tile);  // 0 when m_used = -inf
-          m_used = m_tile;
-        }
-        const float nm = m_used == -INFINITY ? 0.0f : -m_used;
-        float sum[8];
-#pragma unroll
-        for (int i8 = 0; i8 < 8; ++i8) sum[i8] = 0.0f;
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 64; c += 2) {
-          fma2(s[c], s[c + 1], s[c], s[c + 1], sl2, sl2, nm, nm);
-          if ((c & 15) == 14) {
-            exp2_fma_pair(s[c], s[c + 1]);  // one pair in eight on the FMA pipe
-          } else {
-            s[c] = fast_exp2(s[c]);
-            s[c + 1] = fast_exp2(s[c + 1]);
-          }
-          const int k = (c >> 1) & 3;  // four independent accumulator pairs
-          add2(sum[2 * k], sum[2 * k + 1], sum[2 * k], sum[2 * k + 1], s[c], s[c + 1]);
-          pk[c >> 1] = pack_bf16x2(s[c], s[c + 1]);
-        }
-        // keys [64 hf, +64) -> packed columns [32 hf, +32) of this buffer
-        tmem_st32(scol + hf * 32, pk);
-        l = l * alpha + (((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7])));
-        if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-          // O is quiescent once PV_{t-1} has completed (PV_t waits for this
-          // P). Waited on only here: the issuer waited for PV_{t-3} before
-          // S_t, and PV_{t+2} needs this warp's P, so the barrier of buffer
-          // (t-1) % kSBufs is at PV_{t-1}'s phase or one past it.
-          const int pb = (t - 1) % kSBufs;
-          if (!warp_wait(&bars[kPVDone + pb], ((t - 1) / kSBufs) & 1)) {
-            alive = false;
-            break;
-          }
-          tc_fence_after();
-          // this half rescales O columns [64 hf, +64)
-          uint32_t o0[32], o1[32];
-          const uint32_t oaddr = lane_base + kOCol + hf * 64;
-          tmem_ld32(oaddr, o0);
-          tmem_ld32(oaddr + 32, o1);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            o0[c] = __float_as_uint(__uint_as_float(o0[c]) * alpha);
-            o1[c] = __float_as_uint(__uint_as_float(o1[c]) * alpha);
-          }
-          tmem_st32(oaddr, o0);
-          tmem_st32(oaddr + 32, o1);
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        // One P barrier per S buffer: P_{t+3} needs S_{t+3}, hence PV_t, so
-        // the issuer is never two phases behind it.
-        if (lane == 0) mbar_arrive(&bars[kPFull + buf]);
-      }
-      if (!alive) break;
-      // Row sum = both halves' sums; half 0 hands (max used, sum) to the
-      // epilogue (one slot, freed by it).
-      float lo;
-      if (!exchange(l, lo)) break;
-      if (hf == 0) {
-        if (ix > 0 && !warp_wait(&bars[kStatsFree], (ix - 1) & 1)) break;
-        // no finite score seen: the sum holds only clamped-exponent residue
-        stats[r] = make_float2(m_used, m_used == -INFINITY ? 0.0f : l + lo);
-        mbar_arrive(&bars[kStatsFull]);
-      }
-      ++ix;
-    }
+  // Register split: 2 x 128 x kSoftmaxRegs + 2 x 128 x kOtherRegs = 512 x
+  // 128, so every increase is met (the launcher refuses a build whose kernel
+  // does not launch with kLaunchRegs). Each warpgroup executes one setmaxnreg.
+  if (warp >= 4 && warp < 12) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
+    softmax_role(p, bars, ring, stats, tmem, warp, lane);
   } else {
-    // ---------------------------------------------------------- epilogue
-    const int quad = warp & 3;
-    const int r = quad * 32 + lane;
-    const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
-    const int rq = r / p.group;
-    int ix = 0;
-    bool alive = true;
-    Item it;
-    for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
-      const int qpos = it.q0 + rq;
-      const bool valid_row = r < p.rows_used && rq < it.qx && qpos < p.max_q;
-      const int head = it.h * p.group + (r - rq * p.group);
-      __nv_bfloat16* dst = p.out + (((long long)it.q_begin + qpos) * p.qh + head) * 128;
-      float* lse_dst = p.lse ? p.lse + ((long long)it.b * p.qh + head) * p.max_q + qpos : nullptr;
-      if (it.n == 0) {
-        // No visible keys (invalid context): zero rows, -inf LSE.
-        if (valid_row) {
-          for (int d = 0; d < 128; d += 8) *reinterpret_cast<uint4*>(dst + d) = make_uint4(0, 0, 0, 0);
-          if (lse_dst) *lse_dst = -INFINITY;
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kOtherRegs));
+    if (warp == 0) {
+      // ----------------------------------- scheduler, Q and K producer
+      if (lane == 0) {
+        tma_prefetch_desc(&qmap);
+        tma_prefetch_desc(&kmap);
+        tma_prefetch_desc(&vmap);
+        int gt = 0, k_issued = 0, ixq[2] = {0, 0};
+        bool alive = true;
+        for (int i = 0; alive; ++i) {
+          // claim the next item with queries
+          int v;
+          Item it;
+          do {
+            v = atomicAdd(p.sched, 1);
+            if (v >= n_items) break;
+            it = make_item(p, order, v);
+            if (it.qx[0] == 0) {
+              // Pairs past the sequence's queries come first in their group:
+              // move the counter to the group's last (non-empty) pair if
+              // nobody has claimed past this one yet.
+              const int q_len = p.cu_q[it.b + 1] - it.q_begin;
+              const int tiles = q_len > 0 ? p.fd_qt.div(q_len + p.qt - 1) : 0;
+              const int group_end = (p.fd_npair.div(v) + 1) * p.n_pairs;
+              atomicCAS(p.sched, v + 1, group_end - (tiles + 1) / 2);
+            }
+          } while (it.qx[0] == 0);
+          const bool end = v >= n_items;
+          if (end) it.b = -1;
+          if (i >= 2 && !mbar_wait(&bars[kItemEmpty + (i & 1)], ((i >> 1) + 1) & 1, kErrPrefillWait)) break;
+          ring[i & 1] = it;
+          mbar_arrive(&bars[kItemFull + (i & 1)]);
+          if (end) break;
+          const int nt = item_tiles(it);
+          if (nt == 0) continue;  // rows without keys: only the epilogue acts
+#pragma unroll
+          for (int x = 0; x < 2 && alive; ++x) {
+            if (it.n[x] == 0) continue;
+            // Q buffer x is free once the last S MMA of its previous tile completed.
+            if (ixq[x] >= 1 && !mbar_wait(&bars[kQFree + x], (ixq[x] - 1) & 1, kErrPrefillWait)) {
+              alive = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bars[kQFull + x], 2u * 128u * uint32_t(p.rows_used));
+            const int qy = it.h * p.group, qz = it.q_begin + it.q0[x];
+            unsigned char* qdst = tiles + kQOff + x * kQBytes;
+            tma_load_3d(qdst, &qmap, &bars[kQFull + x], 0, qy, qz);
+            tma_load_3d(qdst + kHalf, &qmap, &bars[kQFull + x], 64, qy, qz);
+            ++ixq[x];
+          }
+          const int* table = p.block_table + (long long)it.b * p.table_stride;
+          for (int j = 0; j < nt && alive; ++j) {
+            const int g = gt + j, st = g & 1;
+            const int key0 = j * kKeys;
+            const int logical = p.fd_bs.div(key0);
+            const int page = table[logical];
+            const bool ok = page_ok(page, p.num_blocks);
+            const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
+            if (g >= kKStages && !mbar_wait(&bars[kKEmpty + st], ((g >> 1) + 1) & 1, kErrPrefillWait)) {
+              alive = false;
+              break;
+            }
+            unsigned char* kdst = tiles + kKOff + st * kKVBytes;
+            if (ok) {
+              mbar_arrive_expect_tx(&bars[kKFull + st], kKVBytes);
+              tma_load_3d(kdst, &kmap, &bars[kKFull + st], 0, it.h, trow);
+              tma_load_3d(kdst + kHalf, &kmap, &bars[kKFull + st], 64, it.h, trow);
+            } else {
+              mbar_arrive(&bars[kKFull + st]);
+            }
+            k_issued = g + 1;
+          }
+          gt += nt;
         }
-        continue;
+        // Drain: every copy this thread issued has landed before the CTA
+        // exits (already true on the normal path; bounded on an error path).
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          if (k_issued > s) mbar_wait(&bars[kKFull + s], ((k_issued - 1 - s) >> 1) & 1, kErrPrefillWait);
+          if (ixq[s] > 0) mbar_wait(&bars[kQFull + s], (ixq[s] - 1) & 1, kErrPrefillWait);
+        }
       }
-      if (!warp_wait(&bars[kStatsFull], ix & 1)) break;
-      const float2 ml = stats[r];
-      mbar_arrive(&bars[kStatsFree]);
-      if (!warp_wait(&bars[kODone], ix & 1)) break;
-      tc_fence_after();
-      const float l = ml.y;
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    } else if (warp == 3) {
+      // --------------------------------------------------- V producer
+      if (lane == 0) {
+        tma_prefetch_desc(&vmap);
+        int gt = 0, v_issued = 0;
+        bool alive = true;
+        Item it;
+        for (int i = 0; alive && take_item(bars, ring, i, false, it); ++i) {
+          const int nt = item_tiles(it);
+          const int* table = p.block_table + (long long)it.b * p.table_stride;
+          for (int j = 0; j < nt; ++j) {
+            const int g = gt + j, st = g & 1;
+            const int key0 = j * kKeys;
+            const int logical = p.fd_bs.div(key0);
+            const int page = table[logical];
+            const bool ok = page_ok(page, p.num_blocks);
+            const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
+            if (g >= kVStages && !mbar_wait(&bars[kVEmpty + st], ((g >> 1) + 1) & 1, kErrPrefillWait)) {
+              alive = false;
+              break;
+            }
+            unsigned char* vdst = tiles + kVOff + st * kKVBytes;
+            if (ok) {
+              mbar_arrive_expect_tx(&bars[kVFull + st], kKVBytes);
+              tma_load_3d(vdst, &vmap, &bars[kVFull + st], 0, it.h, trow);
+              tma_load_3d(vdst + kHalf, &vmap, &bars[kVFull + st], 64, it.h, trow);
+            } else {
+              mbar_arrive(&bars[kVFull + st]);
+            }
+            v_issued = g + 1;
+          }
+          gt += nt;
+        }
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t o0[32], o1[32];
-        tmem_ld32(lane_base + kOCol + h * 64, o0);
-        tmem_ld32(lane_base + kOCol + h * 64 + 32, o1);
-        tmem_ld_wait();
-        if (valid_row) {
+        for (int s = 0; s < 2; ++s)
+          if (v_issued > s) mbar_wait(&bars[kVFull + s], ((v_issued - 1 - s) >> 1) & 1, kErrPrefillWait);
+      }
+    } else if (warp == 1) {
+      // --------------------------------------------------- S MMA issuer
+      // Per KV tile j: S_A = Q_A K_j^T, then S_B = Q_B K_j^T. S_x is single-
+      // buffered, so S_x for tile j waits for PV_x of its previous tile (the
+      // P that PV read sits in the same TMEM columns).
+      if (lane == 0) {
+        int gt = 0, tx[2] = {0, 0}, ixq[2] = {0, 0};
+        bool alive = true;
+        // Descriptors of Q buffer 0 and K stage 0; buffers/stages are 2048 16-byte units apart.
+        const uint64_t qd = sw128_desc(sbase + kQOff, 16, 1024), kd = sw128_desc(sbase + kKOff, 16, 1024);
+        const uint32_t q_lo = uint32_t(qd), q_hi = uint32_t(qd >> 32), k_lo = uint32_t(kd), k_hi = uint32_t(kd >> 32);
+        static_assert(kQBytes == kKVBytes && kKVBytes >> 4 == 2048, "stage stride in descriptor units");
+        Item it;
+        for (int i = 0; alive && take_item(bars, ring, i, false, it); ++i) {
+          const int nt = item_tiles(it);
+          for (int j = 0; j < nt && alive; ++j) {
+            const int g = gt + j, ks = g & 1;
+            alive = mbar_wait(&bars[kKFull + ks], (g >> 1) & 1, kErrPrefillWait);
+            const uint32_t kb = k_lo + uint32_t(ks) * 2048u;
 #pragma unroll
-          for (int vv = 0; vv < 8; ++vv) {
-            const uint32_t* src = vv < 4 ? o0 + 8 * vv : o1 + 8 * (vv - 4);
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
-            *reinterpret_cast<uint4*>(dst + h * 64 + vv * 8) = w;
+            for (int x = 0; x < 2 && alive; ++x) {
+              if (j >= it.n[x]) continue;
+              if (j == 0) alive = mbar_wait(&bars[kQFull + x], ixq[x] & 1, kErrPrefillWait);
+              if (alive && tx[x] >= 1) alive = mbar_wait(&bars[kPVDone + x], (tx[x] - 1) & 1, kErrPrefillWait);
+              if (!alive) break;
+              tc_fence_after();
+              const uint32_t qa = q_lo + uint32_t(x) * 2048u, sd = tmem + kSCol + x * kKeys;
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t off = uint32_t((kk >> 2) * kHalf + (kk & 3) * 32) >> 4;
+                umma_ss(sd, qa + off, q_hi, kb + off, k_hi, kIdescS, kk > 0 ? 1u : 0u);
+              }
+              umma_commit(&bars[kSFull + x]);
+              if (j == it.n[x] - 1) {
+                umma_commit(&bars[kQFree + x]);
+                ++ixq[x];
+              }
+              ++tx[x];
+            }
+            if (alive) umma_commit(&bars[kKEmpty + ks]);
+          }
+          gt += nt;
+        }
+        // every MMA issued by this thread completes before TMEM is freed
+        umma_commit(&bars[kDrain]);
+        mbar_wait(&bars[kDrain], 0, kErrPrefillWait);
+      }
+    } else if (warp == 2) {
+      // ---------------------------------------- V fixer and PV issuer
+      // Fixes V_j (zeroes rows that are not real keys: past kv_len or an
+      // invalid page, so P ~ 0 never meets a non-finite cache value), then
+      // lane 0 issues O_A += P_A V_j and O_B += P_B V_j (the S MMAs come from
+      // warp 1: two issuing threads). A tile's first PV also waits for the
+      // epilogue's read of that tile's previous O.
+      int gt = 0, tx[2] = {0, 0}, ixo[2] = {0, 0};
+      bool alive = true;
+      const uint64_t vd = sw128_desc(sbase + kVOff, kHalf, 1024);
+      const uint32_t v_lo = uint32_t(vd), v_hi = uint32_t(vd >> 32);
+      Item it;
+      for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
+        const int nt = item_tiles(it);
+        const int* table = p.block_table + (long long)it.b * p.table_stride;
+        for (int j = 0; j < nt; ++j) {
+          const int g = gt + j, st = g & 1;
+          const int key0 = j * kKeys;
+          const bool ok = page_ok(table[p.fd_bs.div(key0)], p.num_blocks);
+          const int real = ok ? min(kKeys, it.kv_len - key0) : 0;
+          if (!warp_wait(&bars[kVFull + st], (g >> 1) & 1)) {
+            alive = false;
+            break;
+          }
+          if (real < kKeys) {
+            const uint32_t vbase = sbase + kVOff + st * kKVBytes;
+            for (int e = lane; e < (kKeys - real) * 16; e += 32) {
+              const int row = real + (e >> 4), c = e & 15;
+              st_shared_zero16(vbase + (c >> 3) * kHalf + row * 128 + (c & 7) * 16);
+            }
+            fence_proxy_async_smem();
+          }
+          __syncwarp();
+          bool ok_pv = true;
+          if (lane == 0) {
+            const uint32_t vb = v_lo + uint32_t(st) * 2048u;
+#pragma unroll
+            for (int x = 0; x < 2 && ok_pv; ++x) {
+              if (j >= it.n[x]) continue;
+              if (j == 0 && ixo[x] > 0) ok_pv = mbar_wait(&bars[kOFree + x], (ixo[x] - 1) & 1, kErrPrefillWait);
+              if (ok_pv) ok_pv = mbar_wait(&bars[kPFull + x], tx[x] & 1, kErrPrefillWait);
+              if (!ok_pv) break;
+              tc_fence_after();
+              const uint32_t pa = tmem + kSCol + x * kKeys, od = tmem + kOCol + x * kKeys;
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk) {
+                // P: 16 keys = 8 packed columns; V: 16 keys = 2048 bytes of rows
+                umma_ts(od, pa + kk * 8, vb + kk * 128, v_hi, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+              }
+              umma_commit(&bars[kPVDone + x]);
+              if (j == it.n[x] - 1) {
+                umma_commit(&bars[kODone + x]);
+                ++ixo[x];
+              }
+              ++tx[x];
+            }
+            if (ok_pv) umma_commit(&bars[kVEmpty + st]);
+          }
+          if (!__shfl_sync(0xffffffffu, ok_pv, 0)) {
+            alive = false;
+            break;
           }
         }
+        gt += nt;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[kOFree]);
-      if (valid_row && lse_dst) {
-        const float m_out = ml.x == -INFINITY ? 0.0f : ml.x;
-        *lse_dst = l > 0.0f ? (m_out + fast_log2(l)) * kLn2 : -INFINITY;
+      if (lane == 0) {
+        // every PV MMA completes before TMEM is freed
+        umma_commit(&bars[kPVDrain]);
+        mbar_wait(&bars[kPVDrain], 0, kErrPrefillWait);
       }
-      ++ix;
+    } else if (warp >= 12) {
+      // ------------------------------------------------------- epilogue
+      // O_x / l -> BF16 rows and the LSE for tile A, then tile B; frees O_x
+      // for its next tile as soon as it is read.
+      const int quad = warp & 3;
+      const int r = quad * 32 + lane;
+      const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
+      const int rq = r / p.group;
+      const int rh = r - rq * p.group;
+      int ixo[2] = {0, 0};
+      bool alive = true;
+      Item it;
+      for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          if (it.qx[x] == 0) continue;
+          const int qpos = it.q0[x] + rq;
+          const bool valid_row = r < p.rows_used && rq < it.qx[x] && qpos < p.max_q;
+          const int head = it.h * p.group + rh;
+          __nv_bfloat16* dst = p.out + (((long long)it.q_begin + qpos) * p.qh + head) * 128;
+          float* lse_dst = p.lse ? p.lse + ((long long)it.b * p.qh + head) * p.max_q + qpos : nullptr;
+          if (it.n[x] == 0) {
+            // No visible keys (invalid context): zero rows, -inf LSE.
+            if (valid_row) {
+              for (int d = 0; d < 128; d += 8) *reinterpret_cast<uint4*>(dst + d) = make_uint4(0, 0, 0, 0);
+              if (lse_dst) *lse_dst = -INFINITY;
+            }
+            continue;
+          }
+          if (!warp_wait(&bars[kStatsFull + x], ixo[x] & 1)) {
+            alive = false;
+            break;
+          }
+          const float2 ml = stats[x * kRows + r];
+          mbar_arrive(&bars[kStatsFree + x]);
+          if (!warp_wait(&bars[kODone + x], ixo[x] & 1)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+          const float l = ml.y;
+          const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll 1
+          for (int h = 0; h < 8; ++h) {  // 16 columns at a time (this warpgroup runs on kOtherRegs)
+            uint32_t o[16];
+            tmem_ld16(lane_base + kOCol + x * kKeys + h * 16, o);
+            tmem_ld_wait();
+            reg_fence(o);
+            if (valid_row) {
+#pragma unroll
+              for (int vv = 0; vv < 2; ++vv) {
+                const uint32_t* src = o + 8 * vv;
+                uint4 w;
+                w.x = pack_bf16x2(__uint_as_float(src[0]) * inv, __uint_as_float(src[1]) * inv);
+                w.y = pack_bf16x2(__uint_as_float(src[2]) * inv, __uint_as_float(src[3]) * inv);
+                w.z = pack_bf16x2(__uint_as_float(src[4]) * inv, __uint_as_float(src[5]) * inv);
+                w.w = pack_bf16x2(__uint_as_float(src[6]) * inv, __uint_as_float(src[7]) * inv);
+                *reinterpret_cast<uint4*>(dst + h * 16 + vv * 8) = w;
+              }
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[kOFree + x]);
+          if (valid_row && lse_dst) {
+            const float m_out = ml.x == -INFINITY ? 0.0f : ml.x;
+            *lse_dst = l > 0.0f ? (m_out + fast_log2(l)) * kLn2 : -INFINITY;
+          }
+          ++ixo[x];
+        }
+      }
     }
-  }
+  }  // register split
 
   tc_fence_before();
   __syncthreads();
@@ -891,6 +805,9 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   const int group = a.qh / a.kvh;
   if (group < 1 || group > 16 || a.batch > 65535 || a.kvh > 65535) return cudaErrorNotSupported;
   const int qt = kRows / group;
+  // Every sequence within one query tile (chunked prefill of short chunks):
+  // tile B of every pair would be empty, so one tile per item runs faster.
+  if (a.max_q <= qt) return launch_prefill_tile(a, stream);
   PrefillParams p{};
   p.cu_q = a.cu_q;
   p.kv_lens = a.kv_lens;
@@ -931,6 +848,12 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   if (!(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit)) {
     e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
+    // The in-kernel register split assumes exactly kLaunchRegs a thread at
+    // launch; with fewer, a setmaxnreg.inc would wait for registers forever.
+    cudaFuncAttributes fa{};
+    e = cudaFuncGetAttributes(&fa, prefill_kernel);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kLaunchRegs) return cudaErrorInvalidKernelImage;
     __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
   }
   static int sm_count[64] = {};
@@ -943,11 +866,12 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   p.sched = sched_pair(stream, dev, &e);
   if (!p.sched) return e;
   p.n_qtiles = (a.max_q + qt - 1) / qt;
-  p.fd_nqt = FastDiv::make(p.n_qtiles > 0 ? p.n_qtiles : 1);
+  p.n_pairs = (p.n_qtiles + 1) / 2;
+  p.fd_npair = FastDiv::make(p.n_pairs > 0 ? p.n_pairs : 1);
   p.fd_kvh = FastDiv::make(a.kvh);
   p.fd_qt = FastDiv::make(qt);
   p.fd_bs = FastDiv::make(a.block_size);
-  const long long items = (long long)p.n_qtiles * a.batch * a.kvh;
+  const long long items = (long long)p.n_pairs * a.batch * a.kvh;
   if (items > 0x7fffffffLL) return cudaErrorNotSupported;
   const int grid = int(items < sm_count[dev & 63] ? items : sm_count[dev & 63]);
   prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p, *qmap, *kmap, *vmap);

@@ -73,6 +73,17 @@ def test_chunked_prefill_over_cached_prefix(nvb, oracle):
     _check(nvb, oracle, case, what="chunk 64")
 
 
+def test_chunked_prefill_pair_tiles_of_unequal_length(nvb, oracle):
+    # 100-token chunks span two 64-query tiles (16q/8kv): the pair kernel. Over
+    # a 960-token prefix tile A (queries 0-63) visits 8 KV tiles and tile B 9;
+    # a 36-query chunk leaves tile B empty; a 2000-token prefix crosses pages.
+    W = nvb.workloads
+    prefix = [960, 1000, 40, 2000]
+    q_lens = [100, 100, 36, 100]
+    case = W.paged_case([p + q for p, q in zip(prefix, q_lens)], q_lens, q_heads=16, kv_heads=8, seed=8, scale=1.0)
+    _check(nvb, oracle, case, what="chunk 100, unequal pair tiles")
+
+
 @pytest.mark.parametrize("qh,kvh", [(8, 8), (32, 8), (64, 8), (40, 8)])
 def test_prefill_group_sizes(nvb, oracle, qh, kvh):
     W = nvb.workloads
