@@ -412,6 +412,9 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
                                                       const float* __restrict__ out_accum,
                                                       __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
                                                       int rows, int qh, int splits, int lse_stride) {
+  // Launched as a programmatic dependent of the decode grid: wait until that
+  // grid has completed and its partials are visible (a no-op otherwise).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (item >= (long long)rows * qh) return;
@@ -499,9 +502,21 @@ cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream) {
   using namespace decode_detail;
   const long long items = (long long)p.rows * p.qh;
   const long long grid = (items + 7) / 8;
-  combine_kernel<<<unsigned(grid), 256, 0, stream>>>(p.lse_accum, p.out_accum, p.out, p.lse, p.rows, p.qh,
-                                                     p.num_splits, p.max_q);
-  return cudaGetLastError();
+  // Programmatic stream serialization: the combine's launch overlaps the
+  // decode grid's tail instead of following its completion.
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, combine_kernel, static_cast<const float*>(p.lse_accum),
+                            static_cast<const float*>(p.out_accum), p.out, p.lse, p.rows, p.qh, p.num_splits,
+                            p.max_q);
 }
 
 }  // namespace nvb

@@ -128,6 +128,10 @@ __device__ __forceinline__ uint32_t sw_offset(int row, int col, int half_bytes) 
 __global__ void __launch_bounds__(kThreads, 2)
     decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap) {
+  // A split-KV combine launched after this grid with programmatic stream
+  // serialization may be scheduled now; it waits (griddepcontrol.wait) for
+  // this grid to complete before it reads the partials.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
   const uint32_t tile_addr = (raw_addr + kHeadBytes + 1023u) & ~1023u;
