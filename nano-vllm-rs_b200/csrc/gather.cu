@@ -37,6 +37,11 @@ __global__ void __launch_bounds__(256) combine_gather_kernel(const float* __rest
                                                              const __nv_bfloat16* __restrict__ local_out, int rows,
                                                              int qh, int splits, PeerPtrs peers, int world,
                                                              int head_offset, int qh_total) {
+  // Launched as a programmatic dependent of the decode grid (see
+  // nvb_paged_decode_gather): the barrier kernel after it may be scheduled
+  // now, and this grid waits for the decode to complete before reading.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (item >= (long long)rows * qh) return;
@@ -77,6 +82,9 @@ __global__ void __launch_bounds__(256) combine_gather_kernel(const float* __rest
 // One warp: lane p writes this rank's epoch into rank p's flag slot `rank`,
 // then waits until rank p's epoch has arrived in this rank's slot p.
 __global__ void gather_barrier_kernel(PeerPtrs peers, int world, int rank, unsigned int epoch) {
+  // Every store of the combine grid before it is complete and visible before
+  // this rank signals its peers (programmatic dependent launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x;
   if (lane < world) {
     __threadfence_system();
@@ -171,13 +179,26 @@ extern "C" int nvb_paged_decode_gather(void* stream, const void* q, const void* 
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const long long items = (long long)batch * q_heads;
-  combine_gather_kernel<<<unsigned((items + 7) / 8), 256, 0, s>>>(
-      lse_accum, out_accum, static_cast<const __nv_bfloat16*>(out_local), batch, q_heads, partials ? num_splits : 1,
-      peers, world, rank * q_heads, world * q_heads);
-  cudaError_t e = cudaGetLastError();
+  // Both kernels are programmatic dependents of the kernel before them on the
+  // stream, so each launch overlaps its predecessor's tail; each waits in
+  // griddepcontrol.wait for the predecessor to complete.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned((items + 7) / 8));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, combine_gather_kernel, static_cast<const float*>(lse_accum),
+                                     static_cast<const float*>(out_accum),
+                                     static_cast<const __nv_bfloat16*>(out_local), batch, q_heads,
+                                     partials ? num_splits : 1, peers, world, rank * q_heads, world * q_heads);
   if (e == cudaSuccess) {
-    gather_barrier_kernel<<<1, 32, 0, s>>>(peers, world, rank, epoch);
-    e = cudaGetLastError();
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    e = cudaLaunchKernelEx(&cfg, gather_barrier_kernel, peers, world, rank, epoch);
   }
   return cuda_status(e, "gather launch");
 }
