@@ -474,6 +474,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (end) break;
           const int nt = item_tiles(it);
           if (nt == 0) continue;  // rows without keys: only the epilogue acts
+          const int* table = p.block_table + (long long)it.b * p.table_stride;
+          // K tile j of this item into the ring once both S MMAs of tile j-2 read its stage.
+          auto load_k = [&](int j) -> bool {
+            const int g = gt + j, st = g & 1;
+            const int key0 = j * kKeys;
+            const int logical = p.fd_bs.div(key0);
+            const int page = table[logical];
+            const bool ok = page_ok(page, p.num_blocks);
+            const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
+            if (g >= kKStages && !mbar_wait(&bars[kKEmpty + st], ((g >> 1) + 1) & 1, kErrPrefillWait)) return false;
+            unsigned char* kdst = tiles + kKOff + st * kKVBytes;
+            if (ok) {
+              mbar_arrive_expect_tx(&bars[kKFull + st], kKVBytes);
+              tma_load_3d(kdst, &kmap, &bars[kKFull + st], 0, it.h, trow);
+              tma_load_3d(kdst + kHalf, &kmap, &bars[kKFull + st], 64, it.h, trow);
+            } else {
+              mbar_arrive(&bars[kKFull + st]);
+            }
+            k_issued = g + 1;
+            return true;
+          };
+          // The item's first K tile goes out before its Q tiles: its stage is
+          // free two tiles before the previous item ends, the Q buffers only
+          // once that item's last S MMAs have read them.
+          alive = load_k(0);
 #pragma unroll
           for (int x = 0; x < 2 && alive; ++x) {
             if (it.n[x] == 0) continue;
@@ -489,28 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_3d(qdst + kHalf, &qmap, &bars[kQFull + x], 64, qy, qz);
             ++ixq[x];
           }
-          const int* table = p.block_table + (long long)it.b * p.table_stride;
-          for (int j = 0; j < nt && alive; ++j) {
-            const int g = gt + j, st = g & 1;
-            const int key0 = j * kKeys;
-            const int logical = p.fd_bs.div(key0);
-            const int page = table[logical];
-            const bool ok = page_ok(page, p.num_blocks);
-            const int trow = ok ? page * p.block_size + (key0 - logical * p.block_size) : 0;
-            if (g >= kKStages && !mbar_wait(&bars[kKEmpty + st], ((g >> 1) + 1) & 1, kErrPrefillWait)) {
-              alive = false;
-              break;
-            }
-            unsigned char* kdst = tiles + kKOff + st * kKVBytes;
-            if (ok) {
-              mbar_arrive_expect_tx(&bars[kKFull + st], kKVBytes);
-              tma_load_3d(kdst, &kmap, &bars[kKFull + st], 0, it.h, trow);
-              tma_load_3d(kdst + kHalf, &kmap, &bars[kKFull + st], 64, it.h, trow);
-            } else {
-              mbar_arrive(&bars[kKFull + st]);
-            }
-            k_issued = g + 1;
-          }
+          for (int j = 1; j < nt && alive; ++j) alive = load_k(j);
           gt += nt;
         }
         // Drain: every copy this thread issued has landed before the CTA
