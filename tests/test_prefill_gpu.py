@@ -130,3 +130,20 @@ def test_prefill_more_items_than_sms(nvb, oracle):
     W = nvb.workloads
     case = W.paged_case([2500, 1800], [2500, 1800], q_heads=16, kv_heads=8, seed=11, scale=1.0)
     _check(nvb, oracle, case, what="persistent items")
+
+
+@pytest.mark.parametrize("max_q", [130, 64])
+def test_prefill_batch_beyond_ranking_limit(nvb, oracle, max_q):
+    # More sequences than the kernels rank by work at start-up (1,024): items
+    # are claimed in index order. Ragged queries over short cached prefixes
+    # (16q/8kv, 64 queries per tile): up to 130 queries runs the pair kernel,
+    # up to 64 the one-tile kernel.
+    import numpy as np
+
+    W = nvb.workloads
+    rng = np.random.default_rng(12 + max_q)
+    q_lens = rng.integers(1, max_q + 1, size=1100).tolist()
+    q_lens[0] = max_q
+    prefix = rng.integers(0, 201, size=1100).tolist()
+    case = W.paged_case([p + q for p, q in zip(prefix, q_lens)], q_lens, q_heads=16, kv_heads=8, seed=13, scale=1.0)
+    _check(nvb, oracle, case, what=f"1,100 sequences, up to {max_q} queries")
