@@ -52,6 +52,14 @@ def test_config1_decode_vs_oracle(nvb, oracle, splits):
     _check(nvb, oracle, case, splits, what="config1")
 
 
+@pytest.mark.parametrize("splits", [1, 3])
+def test_decode_block_size_512(nvb, oracle, splits):
+    # 512-token pages: four 128-token tiles per page in the tensor-core decode,
+    # with and without split-KV.
+    case = nvb.workloads.paged_case([1500, 513, 2048, 90], q_heads=32, kv_heads=8, block_size=512, seed=19)
+    _check(nvb, oracle, case, splits, what="block 512")
+
+
 def test_config1_auto_splits(nvb, oracle):
     case = nvb.workloads.config1_decode()
     sms = torch.cuda.get_device_properties(0).multi_processor_count

@@ -147,3 +147,14 @@ def test_prefill_batch_beyond_ranking_limit(nvb, oracle, max_q):
     prefix = rng.integers(0, 201, size=1100).tolist()
     case = W.paged_case([p + q for p, q in zip(prefix, q_lens)], q_lens, q_heads=16, kv_heads=8, seed=13, scale=1.0)
     _check(nvb, oracle, case, what=f"1,100 sequences, up to {max_q} queries")
+
+
+@pytest.mark.parametrize("q_lens", [[700, 200, 90], [64, 30, 64]])
+def test_prefill_block_size_512(nvb, oracle, q_lens):
+    # 512-token pages hold four 128-key tiles: the page of tile j is j / 4 and
+    # its first row is offset within the page. [700, 200, 90] queries run the
+    # pair kernel, [64, 30, 64] the one-tile kernel.
+    W = nvb.workloads
+    kv = [700, 1300, 1100]
+    case = W.paged_case(kv, q_lens, q_heads=16, kv_heads=8, block_size=512, seed=17, scale=1.0)
+    _check(nvb, oracle, case, what=f"block 512, q {q_lens}")
