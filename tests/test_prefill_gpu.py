@@ -158,3 +158,28 @@ def test_prefill_block_size_512(nvb, oracle, q_lens):
     kv = [700, 1300, 1100]
     case = W.paged_case(kv, q_lens, q_heads=16, kv_heads=8, block_size=512, seed=17, scale=1.0)
     _check(nvb, oracle, case, what=f"block 512, q {q_lens}")
+
+
+@pytest.mark.parametrize("q_len", [300, 64])
+def test_prefill_concurrent_streams(nvb, q_len):
+    # Two launches that overlap on the GPU, on two streams: each stream has its
+    # own work-claim counters, so each result equals the same launch run
+    # alone. 300-query prompts run the pair kernel, 64-query chunks the
+    # one-tile kernel.
+    W = nvb.workloads
+    cases = [W.paged_case([q_len + p for p in prefix], [q_len] * 6, q_heads=16, kv_heads=8, seed=40 + i, scale=1.0)
+             for i, prefix in enumerate(([0, 100, 900, 40, 2000, 300], [500, 0, 60, 1200, 7, 800]))]
+    alone = [_run(nvb, c)[0] for c in cases]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [torch.empty_like(c.q) for c in cases]
+    torch.cuda.synchronize()
+    for rep in range(3):
+        for c, o, st in zip(cases, outs, streams):
+            with torch.cuda.stream(st):
+                nvb.paged_fwd(c.q, c.k, c.v, o, c.cu_q, c.kv_lens, c.block_table, batch=c.batch, max_q=c.max_q,
+                              max_k=int(c.kv_lens.max()), q_heads=16, kv_heads=8, block_size=c.block_size,
+                              table_stride=c.table_stride, num_blocks=c.num_blocks, stream=st)
+        torch.cuda.synchronize()
+        assert nvb.device_error() == 0
+        for o, a in zip(outs, alone):
+            assert torch.equal(o, a), f"stream result differs from the lone launch (rep {rep})"
