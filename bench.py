@@ -20,7 +20,9 @@ Multi-GPU runs are weak-scaled: each rank decodes its own 256-sequence shard
            --e2e-split) so that one chunk's copies overlap another's
            kernels; one chunk measured fastest.
   prefill  varlen causal prefill TFLOP/s on BASELINE config 2 (32 prompts,
-           lengths U[64, 2048], 16q/8kv), causal FLOPs of visible keys only.
+           lengths U[64, 2048], 16q/8kv), causal FLOPs of visible keys only;
+           `prefill.chunked` is the config's second pass (one 64-token chunk
+           per sequence over a cached prefix P ~ U[256, 2048]).
 
 `--impl reference` times the reference's CPU implementation of the path (the
 FP32 oracle port; the reference's own CPU oracle is Rust and cannot be built
@@ -487,10 +489,9 @@ def main():
         e2e_value = world * step_bytes / (e2e_ms / e2e_steps / 1e3) / 1e9
         del qkv_h, dev_in
 
-    # ---------------- prefill TFLOP/s (config 2), rank-local
-    prefill = None
-    if not args.no_prefill:
-        pc = W.config2_prefill(device=dev, seed=rank)
+    # ---------------- prefill TFLOP/s (config 2: full prompts, then the
+    # chunked pass), rank-local
+    def prefill_leg(pc):
         pout = torch.empty_like(pc.q)
         plse = torch.empty(pc.batch, pc.q_heads, pc.max_q, dtype=torch.float32, device=dev)
         kwp = dict(batch=pc.batch, max_q=pc.max_q, max_k=int(pc.kv_lens.max()), q_heads=16, kv_heads=8,
@@ -518,10 +519,20 @@ def main():
             pms = t.item()
         flops = W.prefill_flops(pc)
         tflops = flops / (pms / 1e3) / 1e12
-        prefill = {"value": round(world * tflops, 2), "unit": "TFLOP/s", "ms_per_step": round(pms, 4),
-                   "flops_per_step_per_gpu": flops, "peak": tc_peak, "frac": round(tflops / tc_peak, 4),
-                   "workload": "config2: varlen causal prefill, 32 prompts L~U[64,2048] (seed = rank), 16q/8kv, "
-                               "FLOPs = 4*128*qh per visible (query, key)"}
+        return {"value": round(world * tflops, 2), "unit": "TFLOP/s", "ms_per_step": round(pms, 4),
+                "flops_per_step_per_gpu": flops, "peak": tc_peak, "frac": round(tflops / tc_peak, 4)}
+
+    prefill = None
+    if not args.no_prefill:
+        prefill = prefill_leg(W.config2_prefill(device=dev, seed=rank))
+        prefill["workload"] = ("config2: varlen causal prefill, 32 prompts L~U[64,2048] (seed = rank), 16q/8kv, "
+                               "FLOPs = 4*128*qh per visible (query, key)")
+        prefill["kernel"] = "prefill_kernel"
+        chunked = prefill_leg(W.config2_chunked(device=dev, seed=rank))
+        chunked["workload"] = ("config2 second pass: one 64-token chunk per sequence over a cached prefix "
+                               "P~U[256,2048] (32 sequences, seed = rank), 16q/8kv")
+        chunked["kernel"] = "prefill_tile_kernel"
+        prefill["chunked"] = chunked
 
     # ---------------- long-context decode (config 5), kv-head sharded for N > 1
     long_ctx = None
