@@ -360,6 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* head = tiles + kTileBytes;
   const int n_items = p.n_pairs * p.batch * p.kvh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The next launch on this stream may start its set-up on SMs this grid leaves.
+  asm volatile("griddepcontrol.launch_dependents;");
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(head);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(head + kTmemSlotOff);
@@ -405,6 +407,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_proxy_async_smem();
   }
+  // Launched as a programmatic dependent of the previous kernel on the
+  // stream: the set-up above touches only this CTA's shared memory and TMEM.
+  // Wait for that kernel to complete, its writes (this stream's claim-counter
+  // reset among them) visible, before any global access.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // Sequences ranked by their work (about q tiles x keys seen), heaviest
   // first, so that dynamic claiming ends with small items (the rank of each
   // sequence is the count of heavier ones; ties by index).
@@ -878,8 +885,17 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   const long long items = (long long)p.n_pairs * a.batch * a.kvh;
   if (items > 0x7fffffffLL) return cudaErrorNotSupported;
   const int grid = int(items < sm_count[dev & 63] ? items : sm_count[dev & 63]);
-  prefill_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p, *qmap, *kmap, *vmap);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, prefill_kernel, p, *qmap, *kmap, *vmap);
 }
 
 }  // namespace nvb
