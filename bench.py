@@ -528,10 +528,19 @@ def main():
         prefill["workload"] = ("config2: varlen causal prefill, 32 prompts L~U[64,2048] (seed = rank), 16q/8kv, "
                                "FLOPs = 4*128*qh per visible (query, key)")
         prefill["kernel"] = "prefill_kernel"
-        chunked = prefill_leg(W.config2_chunked(device=dev, seed=rank))
+        cc = W.config2_chunked(device=dev, seed=rank)
+        chunked = prefill_leg(cc)
         chunked["workload"] = ("config2 second pass: one 64-token chunk per sequence over a cached prefix "
                                "P~U[256,2048] (32 sequences, seed = rank), 16q/8kv")
         chunked["kernel"] = "prefill_tile_kernel"
+        # Per key and kv head a 64-query chunk (16q/8kv) does 64 * 2 * 512
+        # FLOPs against 512 B of K/V: 128 FLOP/byte, below the B200's balance
+        # (~250), so HBM bounds it. Bytes: every visible K/V row once (512 B
+        # per token and kv head), Q in, out back.
+        pbytes = cc.kv_bytes() + 2 * cc.q.numel() * cc.q.element_size()
+        pgbs = pbytes / (chunked["ms_per_step"] / 1e3) / 1e9
+        chunked.update({"bound": "hbm", "bytes_per_step_per_gpu": pbytes, "hbm_gbs": round(pgbs, 1),
+                        "hbm_peak": hbm_peak, "hbm_frac": round(pgbs / hbm_peak, 4)})
         prefill["chunked"] = chunked
 
     # ---------------- long-context decode (config 5), kv-head sharded for N > 1
