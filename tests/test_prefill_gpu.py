@@ -183,3 +183,33 @@ def test_prefill_concurrent_streams(nvb, q_len):
         assert nvb.device_error() == 0
         for o, a in zip(outs, alone):
             assert torch.equal(o, a), f"stream result differs from the lone launch (rep {rep})"
+
+
+@pytest.mark.parametrize("q_len", [300, 64])
+def test_prefill_chain_reads_previous_launch(nvb, q_len):
+    # Each launch waits for the kernel before it on the stream before reading
+    # any input (it starts early only to set up shared memory and TMEM). Here
+    # every launch takes the previous launch's output as its queries, with no
+    # host synchronisation in between: the results equal the same chain run
+    # with a synchronise after each launch, bit for bit. 300-query prompts run
+    # the pair kernel, 64-query chunks the one-tile kernel.
+    W = nvb.workloads
+    c = W.paged_case([q_len + p for p in (0, 700, 90, 1500)], [q_len] * 4, q_heads=16, kv_heads=8, seed=50, scale=1.0)
+    kw = dict(batch=c.batch, max_q=c.max_q, max_k=int(c.kv_lens.max()), q_heads=16, kv_heads=8,
+              block_size=c.block_size, table_stride=c.table_stride, num_blocks=c.num_blocks)
+
+    def chain(sync):
+        bufs = [c.q.clone()] + [torch.empty_like(c.q) for _ in range(4)]
+        for i in range(4):
+            nvb.paged_fwd(bufs[i], c.k, c.v, bufs[i + 1], c.cu_q, c.kv_lens, c.block_table, **kw)
+            if sync:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        return bufs[1:]
+
+    ref = chain(True)
+    for rep in range(3):
+        got = chain(False)
+        assert nvb.device_error() == 0
+        for i, (g, r) in enumerate(zip(got, ref)):
+            assert torch.equal(g, r), f"launch {i} of the chain differs (rep {rep})"
