@@ -9,6 +9,8 @@ import random
 
 import numpy as np
 import pytest
+from hypothesis import given, settings
+from hypothesis import strategies as st
 
 
 @pytest.fixture(scope="module")
@@ -44,6 +46,65 @@ def test_flash_metadata_ragged_prefill_and_decode(H):
 def test_flash_metadata_rejects_invalid_groups(H, positions, seqs, n, msg):
     with pytest.raises(H.HostError, match=msg):
         H.flash_metadata(H.Batch(positions=positions, sequence_ids=seqs), n)
+
+
+def _groups_batch(H, lens, starts):
+    positions, seqs = [], []
+    for s, (n, p0) in enumerate(zip(lens, starts)):
+        positions += range(p0, p0 + n)
+        seqs += [s] * n
+    return H.Batch(positions=positions, sequence_ids=seqs)
+
+
+_groups = st.lists(st.tuples(st.integers(1, 40), st.integers(0, 100_000)), min_size=1, max_size=12)
+
+
+@settings(max_examples=150, deadline=None)
+@given(groups=_groups)
+def test_flash_metadata_property_valid_groups(H, groups):
+    # Any batch of nonempty, in-order groups of consecutive positions: cu_q is
+    # the running row count, kv_len the group's last position + 1, max_q the
+    # longest group (src/model.rs:234-267).
+    lens, starts = [g[0] for g in groups], [g[1] for g in groups]
+    cu, kv, mq = H.flash_metadata(_groups_batch(H, lens, starts), len(groups))
+    assert cu == [0] + np.cumsum(lens).tolist()
+    assert kv == [p0 + n for n, p0 in zip(lens, starts)]
+    assert mq == max(lens)
+
+
+@settings(max_examples=150, deadline=None)
+@given(groups=_groups, pick=st.integers(0, 10**6), delta=st.sampled_from([-2, -1, 1, 2]))
+def test_flash_metadata_property_rejects_a_gap(H, groups, pick, delta):
+    # One position moved inside a group of two or more rows breaks the
+    # consecutive run: rejected like the reference does.
+    lens, starts = [g[0] for g in groups], [g[1] for g in groups]
+    multi = [s for s, n in enumerate(lens) if n >= 2]
+    if not multi:
+        return
+    b = _groups_batch(H, lens, starts)
+    s = multi[pick % len(multi)]
+    row = sum(lens[:s]) + 1 + (pick // 7) % (lens[s] - 1)
+    b.positions[row] += delta
+    with pytest.raises(H.HostError, match="consecutive"):
+        H.flash_metadata(b, len(groups))
+
+
+@settings(max_examples=100, deadline=None)
+@given(groups=_groups.filter(lambda g: len(g) >= 2), pick=st.integers(0, 10**6))
+def test_flash_metadata_property_rejects_groups_out_of_order(H, groups, pick):
+    # Two groups swapped (sequence ids no longer ascending) are rejected.
+    lens, starts = [g[0] for g in groups], [g[1] for g in groups]
+    b = _groups_batch(H, lens, starts)
+    a = pick % (len(groups) - 1)
+    order = list(range(len(groups)))
+    order[a], order[a + 1] = order[a + 1], order[a]
+    rows = []
+    for s in order:
+        r0 = sum(lens[:s])
+        rows += range(r0, r0 + lens[s])
+    b2 = H.Batch(positions=[b.positions[r] for r in rows], sequence_ids=[b.sequence_ids[r] for r in rows])
+    with pytest.raises(H.HostError):
+        H.flash_metadata(b2, len(groups))
 
 
 def test_packed_metadata_alignment_values_and_table_padding(H):
