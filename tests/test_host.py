@@ -152,6 +152,46 @@ def test_packed_metadata_writes_flash_fields(H):
     assert staging[s:e].view(np.int32).tolist() == [7, 2]
 
 
+@settings(max_examples=120, deadline=None)
+@given(data=st.data())
+def test_packed_metadata_property_round_trip(H, data):
+    # Any batch that fits the layout reads back field by field from the
+    # staging bytes: the rows' tokens / positions / sequence ids / slots, each
+    # sequence's table row padded with -1 (0xFF bytes) to the layout stride,
+    # the samples' last indices / temperatures / seeds, cu_q and kv_lens.
+    # The staging buffer starts as random bytes (a reused upload buffer).
+    i32 = st.integers(-(2**31), 2**31 - 1)
+    T, S, C = data.draw(st.integers(1, 48)), data.draw(st.integers(1, 8)), data.draw(st.integers(1, 12))
+    layout = H.MetadataLayout(T, S, C)
+    rows, n = data.draw(st.integers(1, T)), data.draw(st.integers(1, S))
+    bstride, k = data.draw(st.integers(1, C)), data.draw(st.integers(0, S))
+    ints = lambda m: data.draw(st.lists(i32, min_size=m, max_size=m))
+    batch = H.Batch(token_ids=ints(rows), positions=ints(rows), sequence_ids=ints(rows), slot_mapping=ints(rows),
+                    block_tables=data.draw(st.lists(st.integers(-1, 10**6), min_size=n * bstride,
+                                                    max_size=n * bstride)),
+                    table_stride=bstride, last_token_indices=ints(k),
+                    temperatures=data.draw(st.lists(st.floats(0, 2, width=32), min_size=k, max_size=k)),
+                    seeds=data.draw(st.lists(st.integers(0, 2**64 - 1), min_size=k, max_size=k)))
+    cu, kv = ints(n + 1), ints(n)
+    rng = np.random.default_rng(data.draw(st.integers(0, 2**32 - 1)))
+    staging = rng.integers(0, 256, layout.bytes, dtype=np.uint8)
+    layout.pack(staging, batch, n, C, cu_q=cu, kv_lens=kv)
+
+    def field(f, count, dtype):
+        s0 = layout.ranges[f][0]
+        return staging[s0:s0 + count * np.dtype(dtype).itemsize].view(dtype).tolist()
+
+    for f, want in (("tokens", batch.token_ids), ("positions", batch.positions), ("sequences", batch.sequence_ids),
+                    ("slots", batch.slot_mapping), ("last_indices", batch.last_token_indices), ("cu_q", cu),
+                    ("kv_lens", kv)):
+        assert field(f, len(want), np.int32) == want, f
+    tables = np.full((n, C), -1, np.int64)
+    tables[:, :bstride] = np.asarray(batch.block_tables, np.int64).reshape(n, bstride)
+    assert field("tables", n * C, np.int32) == tables.ravel().tolist()
+    assert field("temperatures", k, np.float32) == np.asarray(batch.temperatures, np.float32).tolist()
+    assert field("seeds", k, np.uint64) == batch.seeds
+
+
 LIM = dict(max_batch_tokens=16, max_sequences=4, max_model_len=32, block_size=4, num_blocks=8, table_stride=8,
            vocab_size=100)
 
