@@ -301,7 +301,7 @@ def test_sampling_seed_matches_independent_restatement(H):
         assert H.sampling_seed(base, rid, gen) == _mix(_mix(base) ^ _mix(rid) ^ _mix(gen))
 
 
-@pytest.mark.parametrize("seed", range(5))
+@pytest.mark.parametrize("seed", range(24))
 def test_make_batch_slot_and_table_invariants(H, seed):
     rng = random.Random(seed)
     bs = rng.choice([2, 4, 256])
@@ -337,3 +337,9 @@ def test_make_batch_slot_and_table_invariants(H, seed):
     assert H.validate_batch(b, **lim)[:2] == (len(b.positions), len(segs))
     cu, kv, _ = H.flash_metadata(b, len(segs))
     assert kv == [s.end for s in segs]
+    # one row's slot moved to the same offset of the next page: the row no
+    # longer agrees with its table, and validation says so
+    i = rng.randrange(len(b.positions))
+    b.slot_mapping[i] += bs
+    with pytest.raises(H.HostError, match="disagrees"):
+        H.validate_batch(b, **lim)
