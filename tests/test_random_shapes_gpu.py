@@ -2,7 +2,8 @@
 
 Each seed draws one case that mixes what the fixed cases vary one at a time:
 batch size, context and query lengths, kv heads, GQA group, page size and
-(decode) split count. Same tolerances as the fixed cases: max-abs 2e-2 /
+(decode) split count; the short-chunk sweep keeps every sequence's queries
+within one 128-row tile. Same tolerances as the fixed cases: max-abs 2e-2 /
 mean-abs 2e-3 on the output, 1e-3 / 1e-4 on the LSE.
 """
 import numpy as np
@@ -16,7 +17,7 @@ pytestmark = pytest.mark.gpu
 ORACLE_OPS = 3e9  # multiply-adds the scalar oracle does per case, at most
 
 
-@pytest.mark.parametrize("seed", range(10))
+@pytest.mark.parametrize("seed", range(16))
 def test_decode_random_shape(nvb, oracle, seed):
     rng = np.random.default_rng(1000 + seed)
     kvh = int(rng.choice([1, 2, 4, 8]))
@@ -32,7 +33,7 @@ def test_decode_random_shape(nvb, oracle, seed):
                  what=f"seed {seed}: batch {batch}, {kvh * group}q/{kvh}kv, block {bs}, ctx {ctx.min()}-{ctx.max()}")
 
 
-@pytest.mark.parametrize("seed", range(8))
+@pytest.mark.parametrize("seed", range(12))
 def test_prefill_random_shape(nvb, oracle, seed):
     rng = np.random.default_rng(2000 + seed)
     kvh = int(rng.choice([1, 2, 4, 8]))
@@ -47,3 +48,22 @@ def test_prefill_random_shape(nvb, oracle, seed):
                                     kv_heads=kvh, block_size=bs, seed=seed, scale=1.0)
     prefill_check(nvb, oracle, case,
                   what=f"seed {seed}: batch {batch}, {kvh * group}q/{kvh}kv, block {bs}, q {q_lens.tolist()}")
+
+
+@pytest.mark.parametrize("seed", range(10))
+def test_short_chunk_random_shape(nvb, oracle, seed):
+    # Every sequence's queries fit one 128-row tile (q_len <= 128 / group):
+    # chunked prefill of short chunks over long cached prefixes.
+    rng = np.random.default_rng(3000 + seed)
+    kvh = int(rng.choice([1, 2, 4, 8]))
+    group = int(rng.choice([1, 2, 3, 4, 8, 16]))
+    bs = int(rng.choice([256, 512]))
+    batch = int(rng.integers(1, 41))
+    q_lens = rng.integers(1, 128 // group + 1, size=batch)
+    prefix = rng.integers(0, 3001, size=batch)
+    while (q_lens * (prefix + q_lens)).sum() * kvh * group * 256 > ORACLE_OPS:
+        prefix = prefix // 2
+    case = nvb.workloads.paged_case((prefix + q_lens).tolist(), q_lens.tolist(), q_heads=kvh * group,
+                                    kv_heads=kvh, block_size=bs, seed=seed, scale=1.0)
+    prefill_check(nvb, oracle, case,
+                  what=f"seed {seed}: batch {batch}, {kvh * group}q/{kvh}kv, block {bs}, q <= {128 // group}")
