@@ -121,3 +121,58 @@ def test_oracle_matches_reference_kernel_fixtures(oracle, path):
     import golden_check
 
     golden_check.check(oracle, np.load(path, allow_pickle=False), path.stem)
+
+
+def _from_bf16(bits):
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_varlen_random_shapes_match_numpy(oracle, seed):
+    # The varlen oracle against an independent float64 numpy computation on
+    # random shapes: query i of a q_len group sees keys [0, kv_len - q_len + i]
+    # (src/model.rs:1170-1188) except those on an invalid (-1) page; LSE is the
+    # natural log of the softmax denominator at scale 1/sqrt(128).
+    rng = np.random.default_rng(seed)
+    kvh = int(rng.choice([1, 2, 4]))
+    qh = kvh * int(rng.choice([1, 2, 3, 4]))
+    bs = int(rng.choice([16, 32, 256]))
+    batch = int(rng.integers(1, 5))
+    q_lens = rng.integers(1, 9, size=batch)
+    kv_lens = q_lens + rng.integers(0, 300, size=batch)
+    stride = int(max((kv_lens + bs - 1) // bs))
+    blocks = batch * stride + 2
+    table = rng.permutation(blocks)[:batch * stride].astype(np.int32).reshape(batch, stride)
+    for b in range(batch):
+        used = (kv_lens[b] + bs - 1) // bs
+        table[b, used:] = -1
+        if used > 1 and rng.random() < 0.5:
+            table[b, rng.integers(0, used - 1)] = -1  # a hole in the cached prefix
+    total = int(q_lens.sum())
+    q = oracle.bf16_bits(rng.standard_normal((total, qh, 128)).astype(np.float32))
+    k = oracle.bf16_bits(rng.standard_normal(blocks * bs * kvh * 128).astype(np.float32))
+    v = oracle.bf16_bits(rng.standard_normal(blocks * bs * kvh * 128).astype(np.float32))
+    cu = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
+    out, lse = oracle.attention_varlen(q, k, v, cu, kv_lens, table.ravel(), qh=qh, kvh=kvh, bs=bs, blocks=blocks,
+                                       stride=stride)
+    qf = _from_bf16(q).reshape(total, qh, 128)
+    kf = _from_bf16(k).reshape(blocks * bs, kvh, 128)
+    vf = _from_bf16(v).reshape(blocks * bs, kvh, 128)
+    for b in range(batch):
+        keys = np.arange(kv_lens[b])
+        pages = table[b, keys // bs]
+        slots = pages * bs + keys % bs
+        for i in range(q_lens[b]):
+            row = cu[b] + i
+            vis = (keys <= kv_lens[b] - q_lens[b] + i) & (pages >= 0)
+            for h in range(qh):
+                kh = h // (qh // kvh)
+                if not vis.any():
+                    assert np.all(out[row, h] == 0) and np.isneginf(lse[b, h, i])
+                    continue
+                s = kf[slots[vis], kh] @ qf[row, h] / math.sqrt(128)
+                m = s.max()
+                p = np.exp(s - m)
+                ref = p @ vf[slots[vis], kh] / p.sum()
+                assert np.abs(out[row, h] - ref).max() < 2e-5, (b, i, h)
+                assert abs(lse[b, h, i] - (m + math.log(p.sum()))) < 1e-4, (b, i, h)
