@@ -176,3 +176,67 @@ def test_varlen_random_shapes_match_numpy(oracle, seed):
                 ref = p @ vf[slots[vis], kh] / p.sum()
                 assert np.abs(out[row, h] - ref).max() < 2e-5, (b, i, h)
                 assert abs(lse[b, h, i] - (m + math.log(p.sum()))) < 1e-4, (b, i, h)
+
+
+def _bf16_rne(x):
+    # float32 -> bf16 bits, round to nearest even (finite inputs)
+    u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_fused_rope_cached_matches_float32_numpy(oracle, seed):
+    # The cached fused kernel's oracle against a float32 numpy restatement of
+    # kernels/kernels.cu:166-211, bit for bit: sequential f32 sum of squares,
+    # 1 / sqrt(sum / dim + eps), (x * inv_rms) * w rounded to BF16 (:185),
+    # rotate-half with separately rounded products (:203-204), Q to qout, K
+    # (rotated) and V (copied) to their slot, slots outside the cache skipped,
+    # positions past the table rotated by cos 1 / sin 0.
+    rng = np.random.default_rng(seed)
+    kvh = int(rng.choice([1, 2, 4]))
+    qh = kvh * int(rng.choice([1, 2, 4]))
+    dim = int(rng.choice([64, 128]))
+    bs, blocks, max_pos = 4, 6, 50
+    rows = int(rng.integers(1, 12))
+    half = dim // 2
+    qkv_f = (rng.standard_normal((rows, qh + 2 * kvh, dim)) * rng.choice([0.05, 1.0, 8.0])).astype(np.float32)
+    qkv = oracle.bf16_bits(qkv_f)
+    qw = oracle.bf16_bits((1 + 0.02 * rng.standard_normal(dim)).astype(np.float32))
+    kw = oracle.bf16_bits((1 + 0.02 * rng.standard_normal(dim)).astype(np.float32))
+    positions = rng.integers(0, max_pos + 10, size=rows).astype(np.int32)
+    slots = rng.permutation(bs * blocks + 4)[:rows].astype(np.int32) - 2  # some -2 / -1 / past the cache
+    cache = oracle.rope_cache(max_pos, dim, 1e6)
+    eps = np.float32(1e-6)
+    qout = np.zeros((rows, qh, dim), np.uint16)
+    kc = np.full(bs * blocks * kvh * dim, 0x1234, np.uint16)
+    vc = kc.copy()
+    oracle.qkv_rope(qkv, qw, kw, positions, slots, qout, kc, vc, qh=qh, kvh=kvh, dim=dim, bs=bs, blocks=blocks,
+                    eps=float(eps), rope_cache=cache, max_positions=max_pos)
+
+    x_all = oracle.bits_to_f32(qkv).reshape(rows, qh + 2 * kvh, dim).astype(np.float32)
+    wq, wk = oracle.bits_to_f32(qw).astype(np.float32), oracle.bits_to_f32(kw).astype(np.float32)
+    want_q = np.zeros_like(qout)
+    want_k = np.full_like(kc, 0x1234).reshape(bs * blocks, kvh, dim)
+    want_v = want_k.copy()
+    for r in range(rows):
+        p = int(positions[r])
+        c = cache[p, :half] if p < max_pos else np.ones(half, np.float32)
+        s = cache[p, half:] if p < max_pos else np.zeros(half, np.float32)
+        c, s = np.concatenate([c, c]), np.concatenate([s, s])
+        for head in range(qh + kvh):
+            x = x_all[r, head]
+            total = np.cumsum(x * x, dtype=np.float32)[-1]
+            inv = np.float32(1) / np.sqrt(total / np.float32(dim) + eps)
+            w = wq if head < qh else wk
+            n = oracle.bits_to_f32(_bf16_rne((x * inv) * w)).astype(np.float32)
+            partner = np.concatenate([n[half:], n[:half]])
+            a, b = n * c, partner * s
+            rot = np.concatenate([a[:half] - b[:half], a[half:] + b[half:]])
+            if head < qh:
+                want_q[r, head] = _bf16_rne(rot)
+            elif 0 <= slots[r] < bs * blocks:
+                want_k[slots[r], head - qh] = _bf16_rne(rot)
+                want_v[slots[r], head - qh] = qkv.reshape(rows, qh + 2 * kvh, dim)[r, qh + kvh + head - qh]
+    assert np.array_equal(qout, want_q)
+    assert np.array_equal(kc.reshape(want_k.shape), want_k)
+    assert np.array_equal(vc.reshape(want_v.shape), want_v)
