@@ -182,3 +182,40 @@ def test_rejects_unsupported_head_dim(nvb):
     with pytest.raises(nvb.NvbError, match="head_dim 128"):
         nvb.qkv_rope(t, t, t, i, i, t, t, t, rows=1, q_heads=1, kv_heads=1, head_dim=64, block_size=1,
                      num_blocks=1, eps=EPS, theta=THETA)
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_fused_store_random_shapes_bit_exact_vs_reference_kernel(nvb, ref_native, seed):
+    # Random head counts, row counts, input scales, table lengths, positions
+    # (some before 0 or past the table) and slots (some outside the cache):
+    # Q, the K cache and the V cache equal the reference kernel's bit for bit.
+    rng = np.random.default_rng(4000 + seed)
+    kvh = int(rng.choice([1, 2, 4, 8]))
+    qh = kvh * int(rng.choice([1, 2, 4, 8]))
+    rows = int(rng.integers(1, 600))
+    bs, maxpos = 256, int(rng.integers(16, 4097))
+    blocks = rows // bs + 2
+    scale = float(rng.choice([0.05, 1.0, 8.0]))
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    qkv = (torch.randn(rows, qh + 2 * kvh, DIM, generator=g, device="cuda") * scale).bfloat16()
+    qw = (1 + 0.02 * torch.randn(DIM, generator=g, device="cuda")).bfloat16()
+    kw = (1 + 0.02 * torch.randn(DIM, generator=g, device="cuda")).bfloat16()
+    pos = torch.from_numpy(rng.integers(-3, maxpos + 20, size=rows).astype(np.int32)).cuda()
+    slots_np = rng.permutation(bs * blocks + 8)[:rows].astype(np.int32) - 4
+    slots = torch.from_numpy(slots_np).cuda()
+    table = torch.empty(maxpos, DIM, dtype=torch.float32, device="cuda")
+    nvb.rope_cache(table, maxpos, DIM, THETA)
+    shape = (blocks, bs, kvh, DIM)
+    kc0 = torch.randn(shape, generator=g, device="cuda").bfloat16()
+    vc0 = torch.randn(shape, generator=g, device="cuda").bfloat16()
+    qout, kc, vc = torch.zeros(rows, qh, DIM, dtype=torch.bfloat16, device="cuda"), kc0.clone(), vc0.clone()
+    nvb.qkv_rope_cached(qkv, qw, kw, pos, slots, qout, kc, vc, rows=rows, q_heads=qh, kv_heads=kvh, head_dim=DIM,
+                        block_size=bs, num_blocks=blocks, eps=EPS, rope_cache=table, max_positions=maxpos)
+    rq, rk, rv = torch.zeros_like(qout), kc0.clone(), vc0.clone()
+    ref_native.call("nv_qkv_rope_cached", qkv, qw, kw, pos, slots, rq, rk, rv, rows, qh, kvh, DIM, bs, blocks, EPS,
+                    table, maxpos)
+    torch.cuda.synchronize()
+    what = f"seed {seed}: {rows} rows, {qh}q/{kvh}kv, scale {scale}, table {maxpos}"
+    assert torch.equal(qout.view(torch.int16), rq.view(torch.int16)), f"Q differs ({what})"
+    assert torch.equal(kc.view(torch.int16), rk.view(torch.int16)), f"K cache differs ({what})"
+    assert torch.equal(vc.view(torch.int16), rv.view(torch.int16)), f"V cache differs ({what})"
