@@ -189,7 +189,7 @@ def run_reference(args, rank, world):
     t0 = time.perf_counter()
     step(probe)
     per_seq = (time.perf_counter() - t0) / max(1, threads // 4)
-    budget = 150.0  # seconds for the whole --warmup + --steps run
+    budget = args.ref_budget  # seconds for the whole --warmup + --steps run
     n = int(max(1, min(BATCH, budget / max(1, args.steps + args.warmup) / max(per_seq, 1e-6))))
     data = make(n, 8)
     for _ in range(args.warmup):
@@ -280,6 +280,8 @@ def main():
     ap.add_argument("--e2e-split", type=str, default=None,
                     help="comma-separated chunk sizes in sequences (sum = batch); overrides --e2e-chunks")
     ap.add_argument("--no-long-context", action="store_true")
+    ap.add_argument("--ref-budget", type=float, default=150.0,
+                    help="seconds the reference arm's warm-up and timed steps may take in all")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 256 = config 3; smaller only for profiler captures)")
     args = ap.parse_args()
