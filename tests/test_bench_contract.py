@@ -26,3 +26,15 @@ def test_reference_arm_prints_the_contract_line():
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert "workload" in line["config"]
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    # Under torchrun only rank 0 times the host reference and prints the line;
+    # the other ranks exit 0 without work or output.
+    import os
+
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    run = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--gpus", "2", "--steps",
+                          "2", "--warmup", "1"], cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert run.returncode == 0, run.stderr[-2000:]
+    assert not [ln for ln in run.stdout.splitlines() if ln.startswith("{")]
