@@ -111,6 +111,25 @@ def test_shard_plan_rejects_uneven_heads():
     assert sum(len(S.sequence_shard(7, r, 3)) for r in range(3)) == 7
 
 
+def test_sequence_shards_partition_every_small_batch():
+    # Every batch of 0-64 sequences over 1-8 ranks: the ranks' ranges, in rank
+    # order, tile [0, batch) exactly, and their sizes differ by at most one.
+    S = _load()
+    for world in range(1, 9):
+        for batch in range(65):
+            parts = [S.sequence_shard(batch, r, world) for r in range(world)]
+            assert [i for p in parts for i in p] == list(range(batch)), (batch, world)
+            sizes = [len(p) for p in parts]
+            assert max(sizes) - min(sizes) <= 1, (batch, world)
+    # kv-head shards tile the heads the same way, each rank with its GQA groups
+    for world, kvh, qh in ((1, 8, 64), (2, 8, 64), (4, 8, 32), (8, 8, 64), (2, 2, 16)):
+        shards = [S.HeadShard(r, world, kv_heads=kvh, q_heads=qh) for r in range(world)]
+        assert [h for s in shards for h in s.kv_range] == list(range(kvh))
+        assert [h for s in shards for h in s.q_range] == list(range(qh))
+        for s in shards:
+            assert all(q // (qh // kvh) in s.kv_range for q in s.q_range)
+
+
 class _FakePeerLib:
     """Stands in for the CUDA IPC calls: a handle is the owner's pointer."""
 
