@@ -49,6 +49,15 @@ WORKLOAD = ("config3: paged decode attention, Qwen3-8B attention shape (32q/8kv,
             "256 sequences x ctx 4096 per GPU, seeded N(0,1)*0.5, shuffled page table")
 
 
+def bench_config(batch, world):
+    """The `config` object of the JSON line, identical in both arms."""
+    kv_gb = batch * CTX * KVH * DIM * 2 * 2 / 1e9
+    return {"workload": WORKLOAD if batch == BATCH else WORKLOAD.replace("256 sequences", f"{batch} sequences"),
+            "global_batch": batch * world, "seq_len": CTX,
+            "parallelism": f"dp{world} (independent sequence shards, no collective)",
+            "l2": f"no flush: {kv_gb:.2f} GB of KV per GPU > 126 MB L2"}
+
+
 def bytes_per_seq(ctx=CTX):
     kv = ctx * KVH * DIM * 2 * 2
     q_out = 2 * QH * DIM * 2
@@ -203,8 +212,7 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": BATCH * world, "seq_len": CTX,
-                   "parallelism": f"dp{world}", "l2": "n/a (host)"},
+        "config": bench_config(BATCH, world),
         "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"{n} of 256 sequences (ctx 4096, 32q/8kv) per step, FP32 oracle port of "
                                    f"src/gpu.rs:1430-1466 / kernels/flash_native/smoke.cu:57-81, {threads} threads"},
@@ -220,7 +228,14 @@ def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
     runs split-KV decode on its shard, and the combine kernel stores every
     result into all ranks' outputs over NVLink (nvb_paged_decode_gather: one
     launch pair per step, no NCCL). Returns whole-job GB/s of algorithmic
-    bytes, timed with CUDA events (max over ranks)."""
+    bytes, timed with CUDA events (max over ranks).
+
+    A rank's KV shard is 537 MB / N, which fits the 126 MB L2 from N = 8
+    down to 67 MB: steps rotate over enough independently drawn KV sets that
+    the bytes between two uses of one set exceed three L2s. At N > 1 an
+    untimed step first checks the fused gather against the NCCL all-gather
+    of the same local outputs (decode tolerance, max-abs 2e-2 / mean-abs
+    2e-3) and fails the run on a mismatch."""
     import importlib
 
     import torch
@@ -228,25 +243,48 @@ def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
 
     S = importlib.import_module("nano_vllm_rs_b200.sharding")
     batch, ctx, qh, kvh = 4, 32768, 64, 8
+    l2_bytes = 126 * 2**20
     shard = S.HeadShard(rank, world, kv_heads=kvh, q_heads=qh)
-    case = W.paged_case([ctx] * batch, q_heads=shard.q_local, kv_heads=shard.kv_local, seed=500 + rank, device=dev)
-    run = S.KvHeadShardedDecode(nvb, shard, batch=batch, block_size=256, table_stride=case.table_stride,
-                                num_blocks=case.num_blocks, max_k=ctx, device=dev, fused=world > 1)
+    set_bytes = batch * ctx * shard.kv_local * 512
+    nsets = max(1, -(-3 * l2_bytes // set_bytes))
+    cases = [W.paged_case([ctx] * batch, q_heads=shard.q_local, kv_heads=shard.kv_local, seed=500 + 16 * i + rank,
+                          device=dev) for i in range(nsets)]
+    c0 = cases[0]
+    run = S.KvHeadShardedDecode(nvb, shard, batch=batch, block_size=256, table_stride=c0.table_stride,
+                                num_blocks=c0.num_blocks, max_k=ctx, device=dev, fused=world > 1)
 
-    def once():
+    def once(i):
+        c = cases[i % nsets]
         if world > 1:
-            return run(case.q, case.k, case.v, case.cu_q, case.kv_lens, case.block_table, check=False)
-        return run.local(case.q, case.k, case.v, case.cu_q, case.kv_lens, case.block_table, check=False)
+            return run(c.q, c.k, c.v, c.cu_q, c.kv_lens, c.block_table, check=False)
+        return run.local(c.q, c.k, c.v, c.cu_q, c.kv_lens, c.block_table, check=False)
 
-    for _ in range(5):
-        once()
+    check = None
+    if world > 1:
+        fused_out = once(0).clone()
+        nccl = S.KvHeadShardedDecode(nvb, shard, batch=batch, block_size=256, table_stride=c0.table_stride,
+                                     num_blocks=c0.num_blocks, max_k=ctx, device=dev, fused=False,
+                                     num_splits=run.splits)
+        want = nccl(c0.q, c0.k, c0.v, c0.cu_q, c0.kv_lens, c0.block_table)
+        torch.cuda.synchronize()
+        err = (fused_out.float() - want.float()).abs()
+        t = torch.tensor([err.max().item(), err.mean().item()], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        mx, mn = t.tolist()
+        check = {"vs": "NCCL all-gather of the same local outputs", "max_abs": mx, "mean_abs": mn,
+                 "tolerance": [2e-2, 2e-3]}
+        if not (mx <= 2e-2 and mn <= 2e-3):
+            run.close()
+            raise RuntimeError(f"fused multi-GPU gather differs from the NCCL all-gather: max-abs {mx}, mean-abs {mn}")
+    for i in range(5):
+        once(i)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
-    for _ in range(steps):
-        once()
+    for i in range(steps):
+        once(i)
     b.record(stream)
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / steps
@@ -261,6 +299,8 @@ def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
     total_bytes = batch * ctx * kvh * 512 + 2 * batch * qh * 128 * 2
     return {"value": round(total_bytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 5),
             "splits_per_gpu": run.splits, "kv_heads_per_gpu": shard.kv_local,
+            "l2": f"{nsets} KV sets of {set_bytes / 1e6:.0f} MB per GPU, used in turn",
+            "gather_check": check,
             "collective": ("combine fused with the all-gather: peer stores over NVLink + epoch-flag barrier "
                            "(nvb_paged_decode_gather)") if world > 1 else None,
             "workload": "config5: 4 seqs x ctx 32768, 64q/8kv, kv-head sharded over the GPUs, split-KV per GPU"}
@@ -515,14 +555,20 @@ def main():
         p1.record(stream)
         torch.cuda.synchronize()
         pms = p0.elapsed_time(p1) / psteps
+        flops = W.prefill_flops(pc)
+        total_flops = flops
         if world > 1:
+            # every rank draws its own prompts: sum the work, take the slowest rank's time
             t = torch.tensor([pms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             pms = t.item()
-        flops = W.prefill_flops(pc)
-        tflops = flops / (pms / 1e3) / 1e12
-        return {"value": round(world * tflops, 2), "unit": "TFLOP/s", "ms_per_step": round(pms, 4),
-                "flops_per_step_per_gpu": flops, "peak": tc_peak, "frac": round(tflops / tc_peak, 4)}
+            f = torch.tensor([flops], dtype=torch.float64, device=dev)
+            dist.all_reduce(f, op=dist.ReduceOp.SUM)
+            total_flops = f.item()
+        tflops = total_flops / (pms / 1e3) / 1e12
+        return {"value": round(tflops, 2), "unit": "TFLOP/s", "ms_per_step": round(pms, 4),
+                "flops_per_step_all_gpus": total_flops, "flops_per_step_rank0": flops, "peak": tc_peak,
+                "frac": round(tflops / world / tc_peak, 4)}
 
     prefill = None
     if not args.no_prefill:
@@ -540,7 +586,7 @@ def main():
         # (~250), so HBM bounds it. Bytes: every visible K/V row once (512 B
         # per token and kv head), Q in, out back.
         pbytes = cc.kv_bytes() + 2 * cc.q.numel() * cc.q.element_size()
-        pgbs = pbytes / (chunked["ms_per_step"] / 1e3) / 1e9
+        pgbs = pbytes / (chunked["ms_per_step"] / 1e3) / 1e9  # rank 0's bytes over the slowest rank's time
         chunked.update({"bound": "hbm", "bytes_per_step_per_gpu": pbytes, "hbm_gbs": round(pgbs, 1),
                         "hbm_peak": hbm_peak, "hbm_frac": round(pgbs / hbm_peak, 4)})
         prefill["chunked"] = chunked
@@ -564,10 +610,8 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD if batch == BATCH else WORKLOAD.replace("256 sequences", f"{batch} sequences"),
-                       "global_batch": batch * world, "seq_len": CTX,
-                       "parallelism": f"dp{world} (independent sequence shards, no collective)",
-                       "l2": "no flush: 4.3 GB of KV per GPU >> 126 MB L2", "num_splits": splits},
+            "config": bench_config(batch, world),
+            "num_splits": splits,
             "pct_peak": round(100 * value / world / hbm_peak, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": profile_traffic(),

@@ -88,8 +88,9 @@ int nvb_paged_fwd_ex(void* stream, const void* q, const void* k, const void* v, 
  * sequence, total_q == batch); other arguments as nvb_paged_fwd_ex.
  * Limit: num_splits * batch * q_heads <= 16384 (about 8.1 MB held per GPU
  * until exit); larger calls return -1. All calls on a device share the array,
- * so calls that overlap on the GPU race; the first call on each device looks
- * up the array's address and should come before any stream capture. */
+ * so calls that overlap on the GPU race; the first call in each CUDA context
+ * (normally one per device) looks up the array's address and should come
+ * before any stream capture. */
 int nvb_paged_decode_static_scratch(void* stream, const void* q, const void* k, const void* v,
                                     void* out, const int* cu_q, const int* kv_lens,
                                     const int* block_table, int batch, int max_k, int q_heads,

@@ -80,7 +80,64 @@ struct MapEntry {
 thread_local MapEntry g_maps[32];
 thread_local int g_map_next = 0;
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+std::mutex g_ctx_mutex;
+unsigned long long g_ctx_id[kContextSlots] = {};
+unsigned g_ctx_gen[kContextSlots] = {};
+unsigned g_ctx_gen_next = 0;
+int g_ctx_next = 0;
+
 }  // namespace api_detail
+
+int context_slot(int* slot, unsigned* gen) {
+  using namespace api_detail;
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(ptr);
+    ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(ptr);
+  });
+  if (!get_current || !get_id) return int(cudaErrorNotSupported);
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS) return int(cudaErrorDeviceUninitialized);
+  if (!ctx) {
+    // No context bound to this thread yet: cudaSetDevice binds (and, since
+    // CUDA 12, initialises) the current device's primary context.
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return int(e);
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx) return int(cudaErrorDeviceUninitialized);
+  }
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return int(cudaErrorDeviceUninitialized);
+  std::lock_guard<std::mutex> lock(g_ctx_mutex);
+  for (int i = 0; i < kContextSlots; ++i)
+    if (g_ctx_gen[i] && g_ctx_id[i] == id) {
+      *slot = i;
+      *gen = g_ctx_gen[i];
+      return 0;
+    }
+  // A context not seen before takes the oldest slot.
+  const int i = g_ctx_next;
+  g_ctx_next = (g_ctx_next + 1) % kContextSlots;
+  if (++g_ctx_gen_next == 0) ++g_ctx_gen_next;
+  g_ctx_id[i] = id;
+  g_ctx_gen[i] = g_ctx_gen_next;
+  *slot = i;
+  *gen = g_ctx_gen[i];
+  return 0;
+}
 
 // 3-D BF16 tensor map over [dims[2]][dims[1]][dims[0]] (dims[0] contiguous).
 int make_map_3d(const void* base, const uint64_t dims[3], const uint64_t strides[2], const uint32_t box[3],
@@ -150,7 +207,7 @@ int run_decode(cudaStream_t stream, DecodeParams p, const void* k, const void* v
       if (e == cudaSuccess && p.num_splits > 1 && combine) e = launch_combine(p, stream);
       return cuda_status(e, "decode attention launch");
     }
-    cudaGetLastError();
+    // NotSupported is returned before any launch: no error state to clear.
   }
   if (!combine) return fail("split partials need the tensor-core decode (block_size a multiple of 128)");
   if (int rc = kv_decode_map(k, tokens, p.kvh, &kmap)) return rc;
@@ -187,8 +244,8 @@ int paged_fwd_impl(void* stream, const void* q, const void* k, const void* v, vo
                   kv_heads, block_size, table_stride, num_blocks};
     const cudaError_t e = launch_prefill(a, s);
     if (e != cudaErrorNotSupported) return cuda_status(e, "prefill attention launch");
-    // Shapes the tcgen05 kernel does not cover run one CTA per query row.
-    cudaGetLastError();
+    // Shapes the tcgen05 kernel does not cover run one CTA per query row
+    // (launch_prefill returns NotSupported before launching anything).
     DecodeParams p{};
     p.q = static_cast<const __nv_bfloat16*>(q);
     p.out = static_cast<__nv_bfloat16*>(out);

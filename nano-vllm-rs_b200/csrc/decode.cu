@@ -450,17 +450,12 @@ template <int GC>
 cudaError_t launch_gc(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       cudaStream_t stream) {
   constexpr int bytes = Smem<GC>::kBytes;
-  // The dynamic shared-memory opt-in is per device; remember it per device.
-  static unsigned long long configured = 0;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  // The dynamic shared-memory opt-in belongs to the context; set it once per context.
+  static unsigned configured[kContextSlots] = {};
+  cudaError_t e = once_per_context(configured, [] {
+    return cudaFuncSetAttribute(decode_kernel<GC>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  });
   if (e != cudaSuccess) return e;
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (!(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit)) {
-    e = cudaFuncSetAttribute(decode_kernel<GC>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e != cudaSuccess) return e;
-    __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
-  }
   const long long grid = (long long)p.rows * p.kvh * p.n_hgroups * p.num_splits;
   if (grid <= 0 || grid > 0x7fffffffLL) return cudaErrorInvalidValue;
   decode_kernel<GC><<<unsigned(grid), kThreads, bytes, stream>>>(p, kmap, vmap);

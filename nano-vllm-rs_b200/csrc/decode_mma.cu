@@ -467,19 +467,14 @@ cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& kmap, co
   using namespace decode_mma_detail;
   const int group = p.qh / p.kvh;
   if (p.mode != kModeDecode || group > kN || p.block_size % kTok) return cudaErrorNotSupported;
-  static unsigned long long configured = 0;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  static unsigned configured[kContextSlots] = {};
+  const cudaError_t e = once_per_context(configured, [] {
+    cudaError_t r = cudaFuncSetAttribute(decode_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (r != cudaSuccess) return r;
+    return cudaFuncSetAttribute(decode_mma_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                cudaSharedmemCarveoutMaxShared);
+  });
   if (e != cudaSuccess) return e;
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (!(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit)) {
-    e = cudaFuncSetAttribute(decode_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(decode_mma_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return e;
-    __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
-  }
   const long long grid = (long long)p.rows * p.kvh * p.num_splits;
   if (grid <= 0 || grid > 0x7fffffffLL) return cudaErrorInvalidValue;
   decode_mma_kernel<<<unsigned(grid), kThreads, kSmemBytes, stream>>>(p, kmap, vmap);

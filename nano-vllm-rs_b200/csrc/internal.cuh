@@ -75,6 +75,30 @@ int make_map_3d(const void* base, const uint64_t dims[3], const uint64_t strides
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream);
 cudaError_t launch_prefill_tile(const PrefillArgs& a, cudaStream_t stream);
 
+// Per-context host caches. Device symbol addresses and kernel attributes
+// belong to a CUDA context, not to a device: a host process may run this
+// library under a context it created itself, or recreate the primary context
+// (cudaDeviceReset). context_slot() maps the context current on the calling
+// thread (identified by cuCtxGetId, which no later context reuses) to one of
+// kContextSlots slots; `gen` is new each time a slot is handed to another
+// context, so a value cached under a different gen is stale. Implemented in
+// api.cu.
+constexpr int kContextSlots = 64;
+int context_slot(int* slot, unsigned* gen);
+
+// Runs init() once per context: `seen` holds the gen init last ran under for
+// each slot (zero-initialised; gens start at 1).
+template <class F>
+cudaError_t once_per_context(unsigned* seen, F&& init) {
+  int slot = 0;
+  unsigned gen = 0;
+  if (int rc = context_slot(&slot, &gen)) return cudaError_t(rc);
+  if (__atomic_load_n(&seen[slot], __ATOMIC_ACQUIRE) == gen) return cudaSuccess;
+  const cudaError_t e = init();
+  if (e == cudaSuccess) __atomic_store_n(&seen[slot], gen, __ATOMIC_RELEASE);
+  return e;
+}
+
 // Native-form attention for head dimensions other than 128 (generic.cu).
 cudaError_t launch_generic_attention(const void* q, const void* k, const void* v, void* out, const int* positions,
                                      const int* seq_indices, const int* tables, int rows, int qh, int kvh, int dim,

@@ -781,32 +781,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 // launches the prefill (a launch leaves its pair at zero when it ends).
 __device__ int g_prefill_sched[64][2];
 
-// Pair for (stream, device): streams get their own pair in order of first
+// Pair for (stream, context): streams get their own pair in order of first
 // use; past 64 streams pairs are shared by hash, and launches sharing a pair
 // must not overlap in time.
-int* sched_pair(cudaStream_t stream, int dev, cudaError_t* err) {
+int* sched_pair(cudaStream_t stream, cudaError_t* err) {
   static std::mutex mu;
-  static int* base[64] = {};
-  static cudaStream_t keys_s[64];
-  static int keys_d[64];
-  static int used = 0;
+  static int* base[kContextSlots] = {};
+  static unsigned base_gen[kContextSlots] = {};
+  static cudaStream_t keys[kContextSlots][64];
+  static int used[kContextSlots] = {};
+  int ctx = 0;
+  unsigned gen = 0;
+  if (int rc = context_slot(&ctx, &gen)) {
+    *err = cudaError_t(rc);
+    return nullptr;
+  }
   std::lock_guard<std::mutex> lock(mu);
-  if (!base[dev & 63]) {
+  if (base_gen[ctx] != gen) {
     void* ptr = nullptr;
     *err = cudaGetSymbolAddress(&ptr, g_prefill_sched);
     if (*err != cudaSuccess) return nullptr;
-    base[dev & 63] = static_cast<int*>(ptr);
+    base[ctx] = static_cast<int*>(ptr);
+    base_gen[ctx] = gen;
+    used[ctx] = 0;
   }
   int slot = -1;
-  for (int i = 0; i < used; ++i)
-    if (keys_s[i] == stream && keys_d[i] == dev) slot = i;
-  if (slot < 0 && used < 64) {
-    keys_s[used] = stream;
-    keys_d[used] = dev;
-    slot = used++;
+  for (int i = 0; i < used[ctx]; ++i)
+    if (keys[ctx][i] == stream) slot = i;
+  if (slot < 0 && used[ctx] < 64) {
+    keys[ctx][used[ctx]] = stream;
+    slot = used[ctx]++;
   }
   if (slot < 0) slot = int((reinterpret_cast<uintptr_t>(stream) >> 4) & 63);
-  return base[dev & 63] + 2 * slot;
+  return base[ctx] + 2 * slot;
 }
 
 }  // namespace prefill_detail
@@ -851,22 +858,21 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     if (make_map_3d(a.k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, &kmap)) return cudaErrorInvalidValue;
     if (make_map_3d(a.v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, &vmap)) return cudaErrorInvalidValue;
   }
-  static unsigned long long configured = 0;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (!(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & bit)) {
-    e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
+  static unsigned configured[kContextSlots] = {};
+  cudaError_t e = once_per_context(configured, [] {
+    cudaError_t r = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (r != cudaSuccess) return r;
     // The in-kernel register split assumes exactly kLaunchRegs a thread at
     // launch; with fewer, a setmaxnreg.inc would wait for registers forever.
     cudaFuncAttributes fa{};
-    e = cudaFuncGetAttributes(&fa, prefill_kernel);
-    if (e != cudaSuccess) return e;
-    if (fa.numRegs != kLaunchRegs) return cudaErrorInvalidKernelImage;
-    __atomic_fetch_or(&configured, bit, __ATOMIC_RELEASE);
-  }
+    r = cudaFuncGetAttributes(&fa, prefill_kernel);
+    if (r != cudaSuccess) return r;
+    return fa.numRegs == kLaunchRegs ? cudaSuccess : cudaErrorInvalidKernelImage;
+  });
+  if (e != cudaSuccess) return e;
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
   static int sm_count[64] = {};
   if (!sm_count[dev & 63]) {
     int n = 0;
@@ -874,7 +880,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     sm_count[dev & 63] = n;
   }
-  p.sched = sched_pair(stream, dev, &e);
+  p.sched = sched_pair(stream, &e);
   if (!p.sched) return e;
   p.n_qtiles = (a.max_q + qt - 1) / qt;
   p.n_pairs = (p.n_qtiles + 1) / 2;

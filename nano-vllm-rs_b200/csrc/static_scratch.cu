@@ -19,7 +19,8 @@
 //    cleared between calls. Two calls whose kernels overlap on the GPU (on
 //    different streams, or from different host threads) race on the array;
 //    serialise them on one stream.
-//  * The first call on each device looks up the array's device address with
+//  * The first call in each CUDA context (normally one per device: the
+//    primary context) looks up the array's device address with
 //    cudaGetSymbolAddress (the host-side symbol is only a stand-in and must
 //    never be passed to a kernel). Make that first call before any stream
 //    capture.
@@ -36,22 +37,27 @@ constexpr int kStaticPartials = 16384;
 static __device__ __align__(256) float g_static_partials[kStaticPartials * (128 + 1)];
 
 std::mutex g_addr_mutex;
-float* g_addr[64] = {};
+float* g_addr[kContextSlots] = {};
+unsigned g_addr_gen[kContextSlots] = {};
 
-// Device address of g_static_partials on the current device (looked up once).
+// Device address of g_static_partials in the context current on this thread,
+// looked up once per context: each context that loads the library has its
+// own copy of the array, so an address from another context (another
+// device, a context the host created itself, or a primary context that
+// cudaDeviceReset replaced) must never be reused.
 int static_scratch_address(float** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return int(e);
-  if (dev < 0 || dev >= 64) return int(cudaErrorInvalidDevice);
+  int slot = 0;
+  unsigned gen = 0;
+  if (int rc = context_slot(&slot, &gen)) return rc;
   std::lock_guard<std::mutex> lock(g_addr_mutex);
-  if (!g_addr[dev]) {
+  if (g_addr_gen[slot] != gen) {
     void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_static_partials);
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_partials);
     if (e != cudaSuccess) return int(e);
-    g_addr[dev] = static_cast<float*>(ptr);
+    g_addr[slot] = static_cast<float*>(ptr);
+    g_addr_gen[slot] = gen;
   }
-  *out = g_addr[dev];
+  *out = g_addr[slot];
   return 0;
 }
 

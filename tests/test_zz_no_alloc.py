@@ -68,6 +68,20 @@ def test_static_scratch_matches_regular_entry_two_calls_in_a_row(nvb):
     assert nvb.device_error() == 0
 
 
+def test_static_scratch_at_exactly_its_capacity(nvb):
+    # 16 splits x 32 sequences x 32 heads = 16384 partials: the whole array,
+    # including the last partials and the LSE block behind them, is used.
+    case = nvb.workloads.paged_case([4096] * 31 + [300], q_heads=32, kv_heads=8, seed=9)
+    nvb.clear_device_error()
+    for _ in range(2):
+        got, got_lse = _static(nvb, case, 16)
+        want, want_lse = _regular(nvb, case, 16)
+        torch.cuda.synchronize()
+        assert_close(as_f32(got), as_f32(want), 2e-2, 2e-3, "static vs regular at 16384 partials")
+        assert_close(got_lse.cpu().numpy(), want_lse.cpu().numpy(), 1e-3, 1e-4, "lse at 16384 partials")
+    assert nvb.device_error() == 0
+
+
 def test_static_scratch_rejects_calls_beyond_its_capacity(nvb):
     case = nvb.workloads.paged_case([300] * 8, q_heads=32, kv_heads=8, seed=1)
     out = torch.empty_like(case.q)
