@@ -1,0 +1,200 @@
+/*
+ * nvb_engine.h — C ABI of the continuous-batching engine and the Qwen3 model
+ * runner around the paged-attention path.
+ *
+ * Two libraries:
+ *   libnvb_host.so   nvbe_engine_*: the scheduler (plain C++, no CUDA). It
+ *                    restates the reference's LlmEngine (src/runtime.rs:
+ *                    358-777): admission against free KV pages, prefix
+ *                    reuse, chunked prefill under a token budget, preemption
+ *                    with recomputation, per-request sampling seeds. It
+ *                    drives any model runner through NvbeRunFn, the
+ *                    reference's ModelRunner trait (src/runtime.rs:41-49).
+ *   libnvb_model.so  nvbe_model_*: the Qwen3 forward (src/model.rs:635-818)
+ *                    on one GPU with this library's attention kernels
+ *                    (libnvb.so) behind the attention seam, the reference's
+ *                    device-side batch layout (src/model.rs:271-359), and
+ *                    CUDA-graph replay of decode steps (src/model.rs:959-974).
+ *
+ * Return value convention: 0 on success, -1 on invalid input, or a positive
+ * CUDA / cuBLAS status; the message is in a thread-local buffer
+ * (nvbe_engine_last_error for the engine, nvbe_model_last_error for the
+ * model).
+ */
+#ifndef NVB_ENGINE_H
+#define NVB_ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "nvb_host.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ scheduler */
+
+/* SchedulerConfig (src/runtime.rs:73-121). eos_token_id < 0: no EOS token. */
+typedef struct NvbeSchedulerConfig {
+  size_t block_size;
+  size_t num_blocks;
+  size_t max_sequences;
+  size_t max_model_len;
+  size_t max_batch_tokens;
+  int prefix_caching;
+  int64_t eos_token_id;
+} NvbeSchedulerConfig;
+
+/* Request (src/runtime.rs:51-71). The prompt is borrowed for the call. */
+typedef struct NvbeRequest {
+  uint64_t id;
+  const uint32_t* prompt_token_ids;
+  size_t prompt_len;
+  size_t max_tokens;
+  float temperature;
+  int ignore_eos;
+} NvbeRequest;
+
+enum { NVBE_FINISH_LENGTH = 0, NVBE_FINISH_EOS = 1 };
+
+/* RequestOutput (src/runtime.rs:130-143), written into caller-owned arrays:
+ * token_ids and inter_token_latencies_ms need max_tokens entries each
+ * (inter_token_latencies_ms may be null). */
+typedef struct NvbeRequestOutput {
+  uint32_t* token_ids;
+  size_t num_tokens;
+  size_t prompt_tokens;
+  size_t cached_tokens;
+  double ttft_ms;
+  double latency_ms;
+  double* inter_token_latencies_ms;
+  size_t num_gaps;
+  int finish_reason;
+} NvbeRequestOutput;
+
+/* RunStats (src/runtime.rs:145-170). */
+typedef struct NvbeRunStats {
+  double elapsed_seconds;
+  size_t input_tokens;
+  size_t output_tokens;
+  double output_tokens_per_second;
+  size_t total_requests;
+  size_t cached_tokens;
+  size_t cache_hits;
+  size_t prefill_tokens;
+  size_t decode_tokens;
+  size_t prefill_steps;
+  size_t decode_steps;
+  double prefill_seconds;
+  double decode_seconds;
+  size_t preemptions;
+  size_t peak_kv_blocks;
+  double mean_ttft_ms;
+  double mean_latency_ms;
+  double mean_inter_token_latency_ms;
+} NvbeRunStats;
+
+/* One forward pass: fill sampled[batch->samples]. Nonzero = failure. */
+typedef int (*NvbeRunFn)(void* runner, const NvbhBatch* batch, uint32_t* sampled);
+/* Wait for the runner's device work (may be null). Nonzero = failure. */
+typedef int (*NvbeSyncFn)(void* runner);
+
+typedef struct NvbeEngine NvbeEngine;
+
+/* SchedulerConfig::validate (src/runtime.rs:99-121). */
+int nvbe_scheduler_config_validate(const NvbeSchedulerConfig* config);
+int nvbe_engine_create(const NvbeSchedulerConfig* config, NvbeRunFn run, NvbeSyncFn sync, void* runner,
+                       NvbeEngine** out);
+void nvbe_engine_destroy(NvbeEngine* engine);
+/* LlmEngine::generate (src/runtime.rs:386-409): runs every request to
+ * completion; outputs[i] belongs to requests[i]. A runner failure releases
+ * every page, drops the prefix cache and makes the engine refuse later
+ * calls, as the reference does. */
+int nvbe_engine_generate(NvbeEngine* engine, const NvbeRequest* requests, size_t n, uint64_t seed,
+                         NvbeRequestOutput* outputs, NvbeRunStats* stats);
+/* LlmEngine::clear_prefix_cache (src/runtime.rs:379-384). */
+int nvbe_engine_clear_prefix_cache(NvbeEngine* engine);
+size_t nvbe_engine_blocks_in_use(const NvbeEngine* engine);
+size_t nvbe_engine_cached_keys(const NvbeEngine* engine);
+const char* nvbe_engine_last_error(void);
+
+/* ---------------------------------------------------------- model runner */
+
+/* The Qwen3 fields of config.json the forward uses (src/model.rs:19-49). */
+typedef struct NvbeModelConfig {
+  int hidden_size;
+  int intermediate_size;
+  int num_hidden_layers;
+  int num_attention_heads;
+  int num_key_value_heads;
+  int head_dim;
+  int vocab_size;
+  float rms_norm_eps;
+  float rope_theta;
+  int tie_word_embeddings;
+} NvbeModelConfig;
+
+/* ModelOptions (src/model.rs:151-181); the attention backend is this
+ * library's (the paged kernels of libnvb.so). */
+typedef struct NvbeModelOptions {
+  int device;
+  int block_size;
+  int num_blocks;
+  int max_batch_tokens;
+  int max_sequences;
+  int max_model_len;
+  int cuda_graphs;
+} NvbeModelOptions;
+
+/* Borrowed BF16 device weights, row-major [out, in] like the checkpoint
+ * (src/model.rs:431-504): per layer qkv = q_proj ; k_proj ; v_proj rows and
+ * gate_up = gate_proj ; up_proj rows. lm_head may be null when the
+ * embeddings are tied. Each per-layer field is an array of
+ * num_hidden_layers device pointers. */
+typedef struct NvbeModelWeights {
+  const void* embedding;        /* [vocab, hidden] */
+  const void* final_norm;       /* [hidden] */
+  const void* lm_head;          /* [vocab, hidden] or null */
+  const void* const* input_norm;     /* [hidden] */
+  const void* const* qkv;            /* [(qh + 2 kvh) * dim, hidden] */
+  const void* const* q_norm;         /* [dim] */
+  const void* const* k_norm;         /* [dim] */
+  const void* const* o_proj;         /* [hidden, qh * dim] */
+  const void* const* post_norm;      /* [hidden] */
+  const void* const* gate_up;        /* [2 * intermediate, hidden] */
+  const void* const* down;           /* [hidden, intermediate] */
+} NvbeModelWeights;
+
+typedef struct NvbeModel NvbeModel;
+
+/* QwenModel::load minus the checkpoint reader (src/model.rs:381-591):
+ * allocates the paged K/V caches (num_blocks * block_size tokens per layer)
+ * and the workspace for max_batch_tokens rows, builds the RoPE table, and
+ * creates its own stream and cuBLAS handle on `device`. */
+int nvbe_model_create(const NvbeModelConfig* config, const NvbeModelOptions* options,
+                      const NvbeModelWeights* weights, NvbeModel** out);
+void nvbe_model_destroy(NvbeModel* model);
+/* ModelRunner::run (src/model.rs:924-1003), an NvbeRunFn: validates the
+ * batch, uploads its packed metadata once (asynchronously, from pinned
+ * memory), runs the forward (decode batches replay a CUDA graph per batch
+ * size when cuda_graphs is set) and returns the sampled token ids. */
+int nvbe_model_run(void* model, const NvbhBatch* batch, uint32_t* sampled);
+/* An NvbeSyncFn: waits for the model's stream. */
+int nvbe_model_sync(void* model);
+/* BF16 logits of the sampled rows of the latest run, [samples, vocab]
+ * (QwenModel::last_logits, src/model.rs:608-626); a diagnostic copy. */
+int nvbe_model_last_logits(NvbeModel* model, uint16_t* out, size_t capacity, size_t* samples);
+/* Device pointers of layer `layer`'s K and V caches ([num_blocks,
+ * block_size, kv_heads, head_dim] BF16), for tests. */
+int nvbe_model_kv_cache(NvbeModel* model, int layer, void** k, void** v);
+/* The model's CUDA stream (a cudaStream_t). */
+void* nvbe_model_stream(NvbeModel* model);
+size_t nvbe_model_graph_count(const NvbeModel* model);
+const char* nvbe_model_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVB_ENGINE_H */
