@@ -306,6 +306,69 @@ def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
             "workload": "config5: 4 seqs x ctx 32768, 64q/8kv, kv-head sharded over the GPUs, split-KV per GPU"}
 
 
+def engine_leg(nvb, dev, rank, world, runs=1):
+    """the Qwen3-0.6B engine (28 layers, random weights
+    N(0, 0.02)) generating for 256 requests with prompt ids uniform over the
+    vocabulary, prompt lengths U[128, 1024], max_tokens 512, temperature 0.6
+    Gumbel-max with seed 42, ignore_eos; continuous batching (all 256
+    admitted at once, prefill chunked at 16384 tokens) with graph-replayed
+    decode; one engine replica per GPU, each with its own requests. One
+    untimed run captures the decode graphs and warms cuBLAS; the timed runs
+    are whole generate() calls, host scheduling included. Returns whole-job
+    output tokens per second (sum over ranks / slowest rank)."""
+    import torch
+    import torch.distributed as dist
+
+    M, E = nvb.model, nvb.engine
+    cfg = M.Qwen3Config()
+    n_req, lo, hi, max_tokens = 256, 128, 1024, 512
+    g = torch.Generator().manual_seed(4000 + rank)
+    lens = torch.randint(lo, hi + 1, (n_req,), generator=g).tolist()
+    reqs = [E.Request(id=i, prompt_token_ids=torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist(),
+                      max_tokens=max_tokens, temperature=0.6, ignore_eos=True) for i, n in enumerate(lens)]
+    bs = 256
+    pages = sum(-(-(n + max_tokens) // bs) for n in lens)
+    sched = E.SchedulerConfig(block_size=bs, num_blocks=pages, max_sequences=n_req, max_model_len=hi + max_tokens,
+                              max_batch_tokens=16384)
+    opts = M.ModelOptions(device=dev.index or 0, block_size=bs, num_blocks=pages, max_batch_tokens=16384,
+                          max_sequences=n_req, max_model_len=hi + max_tokens, cuda_graphs=True)
+    weights = M.random_weights(cfg, seed=0, device=dev)
+    model = M.Qwen3Model(cfg, opts, weights)
+    engine = E.LlmEngine(sched, model)
+    engine.generate(reqs, 42)  # untimed: graph capture, cuBLAS warm-up
+    if world > 1:
+        dist.barrier()
+    best = None
+    for _ in range(runs):
+        out = engine.generate(reqs, 42)
+        st = out.stats
+        if best is None or st["elapsed_seconds"] < best["elapsed_seconds"]:
+            best = st
+    engine.close()
+    model.close()
+    del weights
+    t = torch.tensor([best["elapsed_seconds"], best["output_tokens"], best["decode_seconds"], best["decode_tokens"],
+                      best["prefill_seconds"], best["prefill_tokens"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        tmax, tsum = t.clone(), t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        elapsed, out_tok = tmax[0].item(), tsum[1].item()
+        dec_s, dec_tok, pre_s, pre_tok = tmax[2].item(), tsum[3].item(), tmax[4].item(), tsum[5].item()
+    else:
+        elapsed, out_tok, dec_s, dec_tok, pre_s, pre_tok = t.tolist()
+    return {"value": round(out_tok / elapsed, 1), "unit": "output tok/s", "elapsed_s": round(elapsed, 4),
+            "output_tokens": int(out_tok), "decode_tok_s": round(dec_tok / dec_s, 1),
+            "prefill_tok_s": round(pre_tok / pre_s, 1), "decode_steps": best["decode_steps"],
+            "prefill_steps": best["prefill_steps"], "mean_itl_ms": round(best["mean_inter_token_latency_ms"], 4),
+            "workload": ("config4: Qwen3-0.6B random init, 256 requests, prompt U[128,1024] uniform ids, "
+                         "max_tokens 512, T=0.6 Gumbel seed 42, ignore_eos; one replica per GPU"),
+            "path": "LlmEngine (C++ scheduler) -> nvbe_model_run: packed metadata H2D, graph-replayed decode "
+                    "(cuBLAS GEMMs, nvb_qkv_rope_cached, nvb_paged_fwd_ex), sampled ids D2H",
+            "reference_published": {"native": 1734.4, "flash": 3877.8, "unit": "output tok/s",
+                                    "hardware": "RTX 5070 Ti, a different workload (ATTENTION.md:16)"}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -320,6 +383,8 @@ def main():
     ap.add_argument("--e2e-split", type=str, default=None,
                     help="comma-separated chunk sizes in sequences (sum = batch); overrides --e2e-chunks")
     ap.add_argument("--no-long-context", action="store_true")
+    ap.add_argument("--no-engine", action="store_true")
+    ap.add_argument("--engine-runs", type=int, default=1, help="timed generate() calls of the config-4 engine leg")
     ap.add_argument("--ref-budget", type=float, default=150.0,
                     help="seconds the reference arm's warm-up and timed steps may take in all")
     ap.add_argument("--batch", type=int, default=BATCH,
@@ -596,6 +661,11 @@ def main():
     if not args.no_long_context and 8 % world == 0:
         long_ctx = long_context_leg(nvb, W, dev, rank, world, stream)
 
+    # ---------------- config 4 engine, one replica per GPU
+    engine = None
+    if not args.no_engine:
+        engine = engine_leg(nvb, dev, rank, world, runs=args.engine_runs)
+
     # ---------------- CPU baseline (rank 0, N = 1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -623,6 +693,7 @@ def main():
             "tok_s_note": "decode query tokens per second through one attention layer",
             "prefill": prefill,
             "long_context": long_ctx,
+            "engine": engine,
             "e2e": None if e2e_value is None else {
                 "value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms / e2e_steps, 5), "chunks": nch, "chunk_sizes": e2e_sizes,

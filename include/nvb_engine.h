@@ -193,6 +193,32 @@ void* nvbe_model_stream(NvbeModel* model);
 size_t nvbe_model_graph_count(const NvbeModel* model);
 const char* nvbe_model_last_error(void);
 
+/* ------------------------------------------------ per-layer kernels
+ * The forward's non-attention kernels, each replacing the reference's entry
+ * point of the same layer (kernels/kernels.cu:470-500) with an explicit
+ * cudaStream_t instead of its Context*. BF16 outputs are bit-identical to
+ * the reference kernels'. Buffers are device pointers; rows-by-hidden
+ * arrays are contiguous, 16-byte aligned where vector access needs it. */
+/* nv_embedding: out[r] = weight[tokens[r]] (zero for ids outside [0, vocab)). */
+int nvbe_layer_embedding(void* stream, const int* tokens, const void* weight, void* out, int rows, int hidden,
+                         int vocab);
+/* nv_rms: out = x * rsqrt(mean(x^2) + eps) * weight. */
+int nvbe_layer_rms(void* stream, const void* x, const void* weight, void* out, int rows, int hidden, float eps);
+/* nv_add_rms: residual += x (stored BF16), out = rms(residual) * weight. */
+int nvbe_layer_add_rms(void* stream, const void* x, void* residual, const void* weight, void* out, int rows,
+                       int hidden, float eps);
+/* nv_silu: out[r] = silu(packed[r, :I]) * packed[r, I:2I]. */
+int nvbe_layer_silu_mul(void* stream, const void* packed, void* out, int rows, int intermediate);
+/* nv_gather: out[r] = x[indices[r]] (zero for indices outside [0, input_rows)). */
+int nvbe_layer_gather(void* stream, const void* x, const int* indices, void* out, int rows, int hidden,
+                      int input_rows);
+/* nv_sample_parallel: Gumbel-max sampling with the reference's SplitMix64
+ * stream (temperature 0: argmax), ties to the lowest token id. The partial
+ * buffers hold rows * nvbe_sample_partitions(vocab) entries each. */
+int nvbe_sample_partitions(int vocab);
+int nvbe_layer_sample(void* stream, const void* logits, const float* temperatures, const uint64_t* seeds, int* out,
+                      float* partial_scores, int* partial_indices, int rows, int vocab);
+
 #ifdef __cplusplus
 }
 #endif

@@ -355,3 +355,4 @@ def version():
 
 from . import workloads  # noqa: E402  (seeded benchmark inputs)
 from . import engine  # noqa: E402,F401  (continuous-batching scheduler, libnvb_host.so)
+from . import model  # noqa: E402,F401  (Qwen3 runner, libnvb_model.so)

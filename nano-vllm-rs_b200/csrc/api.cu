@@ -16,6 +16,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 
 #include "internal.cuh"
 #include "nvb_attention.h"
@@ -69,16 +70,22 @@ struct MapKey {
   bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
 };
 
-struct MapEntry {
-  MapKey key;
-  CUtensorMap map;
-  bool used;
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    // FNV-1a over the key's bytes (the key is zero-initialised, padding included)
+    const unsigned char* b = reinterpret_cast<const unsigned char*>(&k);
+    uint64_t h = 1469598103934665603ULL;
+    for (size_t i = 0; i < sizeof(MapKey); ++i) h = (h ^ b[i]) * 1099511628211ULL;
+    return size_t(h);
+  }
 };
 
-// A small per-thread cache: descriptors depend only on the base pointer and
-// the geometry, which stay fixed across an engine's steps.
-thread_local MapEntry g_maps[32];
-thread_local int g_map_next = 0;
+// Per-thread descriptor cache: a descriptor depends only on the base pointer
+// and the geometry, which stay fixed across an engine's steps (a 28-layer
+// model uses a few hundred). Descriptors are copied out by value, so a
+// later lookup can never change one a caller already holds.
+constexpr size_t kMaxCachedMaps = 4096;
+thread_local std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
 using CtxGetCurrentFn = CUresult (*)(CUcontext*);
 using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
@@ -139,9 +146,10 @@ int context_slot(int* slot, unsigned* gen) {
   return 0;
 }
 
-// 3-D BF16 tensor map over [dims[2]][dims[1]][dims[0]] (dims[0] contiguous).
+// 3-D BF16 tensor map over [dims[2]][dims[1]][dims[0]] (dims[0] contiguous),
+// copied into *out.
 int make_map_3d(const void* base, const uint64_t dims[3], const uint64_t strides[2], const uint32_t box[3],
-                CUtensorMapSwizzle swizzle, const CUtensorMap** out) {
+                CUtensorMapSwizzle swizzle, CUtensorMap* out) {
   using namespace api_detail;
   MapKey key{};
   key.base = base;
@@ -149,31 +157,29 @@ int make_map_3d(const void* base, const uint64_t dims[3], const uint64_t strides
   std::memcpy(key.strides, strides, sizeof(key.strides));
   std::memcpy(key.box, box, sizeof(key.box));
   key.swizzle = int(swizzle);
-  for (auto& e : g_maps)
-    if (e.used && e.key == key) {
-      *out = &e.map;
-      return 0;
-    }
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *out = it->second;
+    return 0;
+  }
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail("cuTensorMapEncodeTiled is unavailable from the CUDA driver");
-  MapEntry& e = g_maps[g_map_next];
-  g_map_next = (g_map_next + 1) % 32;
-  e.used = false;
-  e.key = key;
+  CUtensorMap map;
   const cuuint32_t elem_strides[3] = {1, 1, 1};
-  const CUresult r = fn(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+  const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
                         elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled failed (%d)", int(r));
-  e.used = true;
-  *out = &e.map;
+  if (g_maps.size() >= kMaxCachedMaps) g_maps.clear();
+  g_maps.emplace(key, map);
+  *out = map;
   return 0;
 }
 
 namespace api_detail {
 
 // Decode tiles: [tokens][kv_heads][128] with a {128, 1, kDecodeTile} box.
-int kv_decode_map(const void* cache, long long tokens, int kvh, const CUtensorMap** out) {
+int kv_decode_map(const void* cache, long long tokens, int kvh, CUtensorMap* out) {
   const uint64_t dims[3] = {128, uint64_t(kvh), uint64_t(tokens)};
   const uint64_t strides[2] = {256, uint64_t(kvh) * 256};
   const uint32_t box[3] = {128, 1, uint32_t(kDecodeTile)};
@@ -183,7 +189,7 @@ int kv_decode_map(const void* cache, long long tokens, int kvh, const CUtensorMa
 constexpr float kScaleLog2 = 1.4426950408889634f / 11.313708498984761f;  // log2(e) / sqrt(128)
 
 // tcgen05 decode tiles: [tokens][kv_heads][128] with a {64, 1, 128} box, 128B swizzle.
-int kv_mma_map(const void* cache, long long tokens, int kvh, const CUtensorMap** out) {
+int kv_mma_map(const void* cache, long long tokens, int kvh, CUtensorMap* out) {
   const uint64_t dims[3] = {128, uint64_t(kvh), uint64_t(tokens)};
   const uint64_t strides[2] = {256, uint64_t(kvh) * 256};
   const uint32_t box[3] = {64, 1, 128};
@@ -195,14 +201,13 @@ int kv_mma_map(const void* cache, long long tokens, int kvh, const CUtensorMap**
 // decode can stop there.
 int run_decode(cudaStream_t stream, DecodeParams p, const void* k, const void* v, bool combine = true) {
   const long long tokens = (long long)p.num_blocks * p.block_size;
-  const CUtensorMap* kmap = nullptr;
-  const CUtensorMap* vmap = nullptr;
+  CUtensorMap kmap, vmap;
   p.scale_log2 = kScaleLog2;
   if (p.mode == kModeDecode && p.block_size % 128 == 0 && p.qh / p.kvh <= 16) {
     if (int rc = kv_mma_map(k, tokens, p.kvh, &kmap)) return rc;
     if (int rc = kv_mma_map(v, tokens, p.kvh, &vmap)) return rc;
     p.n_hgroups = 1;
-    cudaError_t e = launch_decode_mma(p, *kmap, *vmap, stream);
+    cudaError_t e = launch_decode_mma(p, kmap, vmap, stream);
     if (e != cudaErrorNotSupported) {
       if (e == cudaSuccess && p.num_splits > 1 && combine) e = launch_combine(p, stream);
       return cuda_status(e, "decode attention launch");
@@ -213,7 +218,7 @@ int run_decode(cudaStream_t stream, DecodeParams p, const void* k, const void* v
   if (int rc = kv_decode_map(k, tokens, p.kvh, &kmap)) return rc;
   if (int rc = kv_decode_map(v, tokens, p.kvh, &vmap)) return rc;
   p.scale_log2 = kScaleLog2;
-  return cuda_status(launch_decode(p, *kmap, *vmap, stream), "decode attention launch");
+  return cuda_status(launch_decode(p, kmap, vmap, stream), "decode attention launch");
 }
 
 int paged_fwd_impl(void* stream, const void* q, const void* k, const void* v, void* out, const int* cu_q,

@@ -64,9 +64,9 @@ struct PrefillArgs {
 };
 
 // Host-side TMA descriptor helper (api.cu): 3-D BF16 map over
-// [dims[2]][dims[1]][dims[0]], cached per thread.
+// [dims[2]][dims[1]][dims[0]], cached per thread, copied into *out.
 int make_map_3d(const void* base, const uint64_t dims[3], const uint64_t strides[2],
-                const uint32_t box[3], CUtensorMapSwizzle swizzle, const CUtensorMap** out);
+                const uint32_t box[3], CUtensorMapSwizzle swizzle, CUtensorMap* out);
 
 // Returns cudaErrorNotSupported when the tcgen05 path does not cover the shape.
 // launch_prefill picks the kernel: pairs of query tiles per work item

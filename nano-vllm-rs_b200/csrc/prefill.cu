@@ -844,7 +844,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   p.num_blocks = a.num_blocks;
   p.scale_log2 = 1.4426950408889634f / 11.313708498984761f;
 
-  const CUtensorMap *qmap = nullptr, *kmap = nullptr, *vmap = nullptr;
+  CUtensorMap qmap, kmap, vmap;
   {
     const uint64_t dims[3] = {128, uint64_t(a.qh), uint64_t(a.total_q)};
     const uint64_t strides[2] = {256, uint64_t(a.qh) * 256};
@@ -901,7 +901,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, prefill_kernel, p, *qmap, *kmap, *vmap);
+  return cudaLaunchKernelEx(&cfg, prefill_kernel, p, qmap, kmap, vmap);
 }
 
 }  // namespace nvb

@@ -786,7 +786,7 @@ cudaError_t launch_prefill_tile(const PrefillArgs& a, cudaStream_t stream) {
   p.num_blocks = a.num_blocks;
   p.scale_log2 = 1.4426950408889634f / 11.313708498984761f;
 
-  const CUtensorMap *qmap = nullptr, *kmap = nullptr, *vmap = nullptr;
+  CUtensorMap qmap, kmap, vmap;
   {
     const uint64_t dims[3] = {128, uint64_t(a.qh), uint64_t(a.total_q)};
     const uint64_t strides[2] = {256, uint64_t(a.qh) * 256};
@@ -835,7 +835,7 @@ cudaError_t launch_prefill_tile(const PrefillArgs& a, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, prefill_tile_kernel, p, *qmap, *kmap, *vmap);
+  return cudaLaunchKernelEx(&cfg, prefill_tile_kernel, p, qmap, kmap, vmap);
 }
 
 }  // namespace nvb

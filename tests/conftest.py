@@ -101,6 +101,23 @@ def ref_native():
     return RefNative(path)
 
 
+@pytest.fixture(scope="session")
+def ref_flash():
+    """The reference's FA2 adapter (oracle/_ref/libref_flash.so, built from
+    kernels/flash_native/flash_native.cu and its vendored FA2 / CUTLASS)."""
+    path = ROOT / "oracle" / "_ref" / "libref_flash.so"
+    if not path.exists():
+        pytest.skip("the reference FA2 adapter was not built (oracle/_ref)")
+    P, I = ctypes.c_void_p, ctypes.c_int
+    L = ctypes.CDLL(str(path))
+    L.nvr_flash_fwd.argtypes = [P] * 8 + [I] * 9 + [P] * 3
+    L.nvr_flash_fwd.restype = I
+    L.nvr_flash_num_splits.argtypes = [I] * 5
+    L.nvr_flash_num_splits.restype = I
+    L.nvr_flash_last_error.restype = ctypes.c_char_p
+    return L
+
+
 @pytest.fixture(autouse=True)
 def _gpu_guard(request):
     if request.node.get_closest_marker("gpu"):

@@ -31,20 +31,6 @@ P, I = ctypes.c_void_p, ctypes.c_int
 RESULTS = {}
 
 
-@pytest.fixture(scope="module")
-def ref_flash():
-    path = ROOT / "oracle" / "_ref" / "libref_flash.so"
-    if not path.exists():
-        pytest.skip("the reference FA2 adapter was not built (oracle/_ref)")
-    L = ctypes.CDLL(str(path))
-    L.nvr_flash_fwd.argtypes = [P] * 8 + [I] * 9 + [P] * 3
-    L.nvr_flash_fwd.restype = I
-    L.nvr_flash_num_splits.argtypes = [I] * 5
-    L.nvr_flash_num_splits.restype = I
-    L.nvr_flash_last_error.restype = ctypes.c_char_p
-    return L
-
-
 def _p(t):
     return P(t.data_ptr()) if t is not None else P(0)
 
