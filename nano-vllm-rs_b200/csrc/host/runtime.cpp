@@ -71,6 +71,7 @@ struct NvbhBlockPool {
   std::vector<Block> blocks;
   std::unordered_map<uint64_t, std::vector<int>> by_hash;
   uint64_t clock = 0;
+  size_t free_count = 0;  // pages with no references, kept so available() is O(1)
 
   void touch(int b) {
     if (clock != std::numeric_limits<uint64_t>::max()) ++clock;  // saturating, as the reference
@@ -244,7 +245,10 @@ int nvbh_validate_batch(const NvbhBatch* b, const NvbhLimits* lim, size_t* rows_
 
 NvbhBlockPool* nvbh_pool_create(size_t num_blocks) {
   NvbhBlockPool* p = new (std::nothrow) NvbhBlockPool();
-  if (p) p->blocks.resize(num_blocks);
+  if (p) {
+    p->blocks.resize(num_blocks);
+    p->free_count = num_blocks;
+  }
   return p;
 }
 
@@ -263,6 +267,7 @@ int nvbh_pool_allocate(NvbhBlockPool* p) {
   if (best < 0) return -1;
   p->invalidate(best);
   p->blocks[size_t(best)].references = 1;
+  p->free_count -= 1;
   p->touch(best);
   return best;
 }
@@ -270,6 +275,7 @@ int nvbh_pool_allocate(NvbhBlockPool* p) {
 void nvbh_pool_release(NvbhBlockPool* p, int block) {
   if (block < 0 || size_t(block) >= p->blocks.size() || p->blocks[size_t(block)].references == 0) return;
   p->blocks[size_t(block)].references -= 1;
+  if (p->blocks[size_t(block)].references == 0) p->free_count += 1;
   p->touch(block);
 }
 
@@ -278,6 +284,7 @@ int nvbh_pool_find(const NvbhBlockPool* p, const uint32_t* tokens, size_t n) { r
 int nvbh_pool_find_and_retain(NvbhBlockPool* p, const uint32_t* tokens, size_t n) {
   const int b = p->find(tokens, n);
   if (b < 0) return -1;
+  if (p->blocks[size_t(b)].references == 0) p->free_count -= 1;
   p->blocks[size_t(b)].references += 1;
   p->touch(b);
   return b;
@@ -294,11 +301,7 @@ void nvbh_pool_publish(NvbhBlockPool* p, int block, const uint32_t* prefix, size
   p->touch(block);
 }
 
-size_t nvbh_pool_available(const NvbhBlockPool* p) {
-  size_t n = 0;
-  for (const auto& b : p->blocks) n += b.references == 0;
-  return n;
-}
+size_t nvbh_pool_available(const NvbhBlockPool* p) { return p->free_count; }
 
 size_t nvbh_pool_in_use(const NvbhBlockPool* p) { return p->blocks.size() - nvbh_pool_available(p); }
 

@@ -11,7 +11,8 @@
 //   silu_mul         kernels.cu:355-364  one BF16 rounding of
 //                    gate / (1 + expf(-gate)) * up
 //   gather           kernels.cu:365-370  row gather (0 for indices out of range)
-// The layouts are this library's own: one warp per row for the norms, 16-byte
+// The layouts are this library's own: 128 threads per row for the norms
+// (one warp per row for hidden sizes that are not a multiple of 256), 16-byte
 // vector accesses elsewhere.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -88,6 +89,79 @@ __global__ void rms_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* _
   }
 }
 
+// RMSNorm with 128 threads per row, for hidden = 256 * NV (NV <= 8): the
+// same sum as rms_kernel, laid out for parallelism. Thread r plays the
+// reference threads r and r + 128: it loads all 2 * NV of their elements at
+// once (kept in registers for the output pass), forms each thread's partial
+// with the same fused multiply-add chain, folds the two partials across its
+// warp (reference warps w and w + 4 for warp w), and the eight warp sums
+// meet in shared memory in the reference's order.
+template <bool ADD, int NV>
+__global__ void __launch_bounds__(128) rms_row_kernel(const __nv_bfloat16* __restrict__ x,
+                                                      __nv_bfloat16* __restrict__ residual,
+                                                      const __nv_bfloat16* __restrict__ weight,
+                                                      __nv_bfloat16* __restrict__ out, int hidden, float eps) {
+  const long long base = (long long)blockIdx.x * hidden;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float v[2][NV];
+#pragma unroll
+  for (int s = 0; s < 2; ++s)
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = tid + 128 * s + 256 * i;
+      float a = bf(x[base + j]);
+      if (ADD) a += bf(residual[base + j]);
+      v[s][i] = a;
+    }
+  float p[2];
+#pragma unroll
+  for (int s = 0; s < 2; ++s) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) acc = __fmaf_rn(v[s][i], v[s][i], acc);
+    p[s] = acc;
+  }
+#pragma unroll
+  for (int s = 0; s < 2; ++s)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) p[s] = __fadd_rn(p[s], __shfl_xor_sync(0xffffffffu, p[s], off));
+  __shared__ float wsum[8];
+  if (lane == 0) {
+    wsum[warp] = p[0];
+    wsum[warp + 4] = p[1];
+  }
+  __syncthreads();
+  const float total = __fadd_rn(__fadd_rn(__fadd_rn(wsum[0], wsum[4]), __fadd_rn(wsum[2], wsum[6])),
+                                __fadd_rn(__fadd_rn(wsum[1], wsum[5]), __fadd_rn(wsum[3], wsum[7])));
+  const float inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(total, float(hidden)), eps));
+#pragma unroll
+  for (int s = 0; s < 2; ++s)
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = tid + 128 * s + 256 * i;
+      if (ADD) residual[base + j] = __float2bfloat16_rn(v[s][i]);
+      const float normalized = __fmul_rn(v[s][i], inv_rms);
+      out[base + j] = __float2bfloat16_rn(__fmul_rn(normalized, bf(weight[j])));
+    }
+}
+
+template <bool ADD>
+cudaError_t launch_rms_rows(cudaStream_t s, const __nv_bfloat16* x, __nv_bfloat16* residual,
+                            const __nv_bfloat16* w, __nv_bfloat16* out, int rows, int hidden, float eps) {
+  switch (hidden / 256) {
+#define NVB_RMS_CASE(NV) \
+  case NV:               \
+    rms_row_kernel<ADD, NV><<<rows, 128, 0, s>>>(x, residual, w, out, hidden, eps); \
+    break;
+    NVB_RMS_CASE(1) NVB_RMS_CASE(2) NVB_RMS_CASE(3) NVB_RMS_CASE(4)
+    NVB_RMS_CASE(5) NVB_RMS_CASE(6) NVB_RMS_CASE(7) NVB_RMS_CASE(8)
+#undef NVB_RMS_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 // SiLU(gate) * up over the packed [rows, 2 * inter] GEMM output, 8 outputs a thread.
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ packed, __nv_bfloat16* __restrict__ out, int rows,
                                 int inter) {
@@ -148,6 +222,10 @@ cudaError_t launch_rms(cudaStream_t s, const void* x, void* residual, const void
   const auto* xp = static_cast<const __nv_bfloat16*>(x);
   const auto* wp = static_cast<const __nv_bfloat16*>(weight);
   auto* op = static_cast<__nv_bfloat16*>(out);
+  if (hidden % 256 == 0 && hidden <= 2048 && rows <= 0x7fffffff) {
+    return residual ? launch_rms_rows<true>(s, xp, static_cast<__nv_bfloat16*>(residual), wp, op, rows, hidden, eps)
+                    : launch_rms_rows<false>(s, xp, nullptr, wp, op, rows, hidden, eps);
+  }
   if (residual)
     rms_kernel<true><<<blocks, 32 * kWarps, 0, s>>>(xp, static_cast<__nv_bfloat16*>(residual), wp, op, rows, hidden,
                                                    eps);
