@@ -188,11 +188,12 @@ int kv_decode_map(const void* cache, long long tokens, int kvh, CUtensorMap* out
 
 constexpr float kScaleLog2 = 1.4426950408889634f / 11.313708498984761f;  // log2(e) / sqrt(128)
 
-// tcgen05 decode tiles: [tokens][kv_heads][128] with a {64, 1, 128} box, 128B swizzle.
-int kv_mma_map(const void* cache, long long tokens, int kvh, CUtensorMap* out) {
+// tcgen05 decode tiles: [tokens][kv_heads][128] with a {64, 1, rows} box
+// (rows 128, or 64 for short last tiles), 128B swizzle.
+int kv_mma_map(const void* cache, long long tokens, int kvh, CUtensorMap* out, uint32_t rows = 128) {
   const uint64_t dims[3] = {128, uint64_t(kvh), uint64_t(tokens)};
   const uint64_t strides[2] = {256, uint64_t(kvh) * 256};
-  const uint32_t box[3] = {64, 1, 128};
+  const uint32_t box[3] = {64, 1, rows};
   return make_map_3d(cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, out);
 }
 
@@ -206,8 +207,11 @@ int run_decode(cudaStream_t stream, DecodeParams p, const void* k, const void* v
   if (p.mode == kModeDecode && p.block_size % 128 == 0 && p.qh / p.kvh <= 16) {
     if (int rc = kv_mma_map(k, tokens, p.kvh, &kmap)) return rc;
     if (int rc = kv_mma_map(v, tokens, p.kvh, &vmap)) return rc;
+    CUtensorMap khalf, vhalf;
+    if (int rc = kv_mma_map(k, tokens, p.kvh, &khalf, 64)) return rc;
+    if (int rc = kv_mma_map(v, tokens, p.kvh, &vhalf, 64)) return rc;
     p.n_hgroups = 1;
-    cudaError_t e = launch_decode_mma(p, kmap, vmap, stream);
+    cudaError_t e = launch_decode_mma(p, kmap, vmap, khalf, vhalf, stream);
     if (e != cudaErrorNotSupported) {
       if (e == cudaSuccess && p.num_splits > 1 && combine) e = launch_combine(p, stream);
       return cuda_status(e, "decode attention launch");

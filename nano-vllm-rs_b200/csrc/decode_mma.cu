@@ -127,7 +127,8 @@ __device__ __forceinline__ uint32_t sw_offset(int row, int col, int half_bytes) 
 
 __global__ void __launch_bounds__(kThreads, 2)
     decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
-                      const __grid_constant__ CUtensorMap vmap) {
+                      const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap kmap_half,
+                      const __grid_constant__ CUtensorMap vmap_half) {
   // A split-KV combine launched after this grid with programmatic stream
   // serialization may be scheduled now; it waits (griddepcontrol.wait) for
   // this grid to complete before it reads the partials.
@@ -228,6 +229,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
+      tma_prefetch_desc(&kmap_half);
+      tma_prefetch_desc(&vmap_half);
       const uint64_t policy = policy_evict_first();
       for (int i = 0; i < ntiles; ++i) {
         const int token0 = (t0 + i) * kTok;
@@ -235,22 +238,30 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int page = table[logical];
         const bool ok = page >= 0 && page < p.num_blocks;
         const int trow = ok ? page * p.block_size + (token0 - logical * p.block_size) : 0;
+        // A sequence's last tile with at most 64 live tokens loads only its
+        // first 64 rows (the rest of the stage is stale and masked: scores
+        // of tokens past the length are dropped and their V rows zeroed),
+        // which halves the bytes read past the end of ragged contexts.
+        const bool half = len - token0 <= kTok / 2;
+        const CUtensorMap* km = half ? &kmap_half : &kmap;
+        const CUtensorMap* vm = half ? &vmap_half : &vmap;
+        const uint32_t tile_bytes = half ? kKVBytes / 2 : kKVBytes;
         const int ks = i % kKStages, vs = i % kVStages;
         if (i >= kKStages && !mbar_wait(&bars[kKEmpty + ks], ((i / kKStages) + 1) & 1, kErrDecodeEmptyWait)) break;
         if (ok) {
           unsigned char* kd = tiles + kKOff + ks * kKVBytes;
-          mbar_arrive_expect_tx(&bars[kKFull + ks], kKVBytes);
-          tma_load_3d_hint(kd, &kmap, &bars[kKFull + ks], 0, kvhead, trow, policy);
-          tma_load_3d_hint(kd + kHalf, &kmap, &bars[kKFull + ks], 64, kvhead, trow, policy);
+          mbar_arrive_expect_tx(&bars[kKFull + ks], tile_bytes);
+          tma_load_3d_hint(kd, km, &bars[kKFull + ks], 0, kvhead, trow, policy);
+          tma_load_3d_hint(kd + kHalf, km, &bars[kKFull + ks], 64, kvhead, trow, policy);
         } else {
           mbar_arrive(&bars[kKFull + ks]);
         }
         if (i >= kVStages && !mbar_wait(&bars[kVEmpty + vs], ((i / kVStages) + 1) & 1, kErrDecodeEmptyWait)) break;
         if (ok) {
           unsigned char* vd = tiles + kVOff + vs * kKVBytes;
-          mbar_arrive_expect_tx(&bars[kVFull + vs], kKVBytes);
-          tma_load_3d_hint(vd, &vmap, &bars[kVFull + vs], 0, kvhead, trow, policy);
-          tma_load_3d_hint(vd + kHalf, &vmap, &bars[kVFull + vs], 64, kvhead, trow, policy);
+          mbar_arrive_expect_tx(&bars[kVFull + vs], tile_bytes);
+          tma_load_3d_hint(vd, vm, &bars[kVFull + vs], 0, kvhead, trow, policy);
+          tma_load_3d_hint(vd + kHalf, vm, &bars[kVFull + vs], 64, kvhead, trow, policy);
         } else {
           mbar_arrive(&bars[kVFull + vs]);
         }
@@ -463,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // Returns cudaErrorNotSupported for shapes this kernel does not cover
 // (groups above 16 query heads, pages that are not a multiple of 128 tokens).
 cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
-                              cudaStream_t stream) {
+                              const CUtensorMap& kmap_half, const CUtensorMap& vmap_half, cudaStream_t stream) {
   using namespace decode_mma_detail;
   const int group = p.qh / p.kvh;
   if (p.mode != kModeDecode || group > kN || p.block_size % kTok) return cudaErrorNotSupported;
@@ -477,7 +488,7 @@ cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& kmap, co
   if (e != cudaSuccess) return e;
   const long long grid = (long long)p.rows * p.kvh * p.num_splits;
   if (grid <= 0 || grid > 0x7fffffffLL) return cudaErrorInvalidValue;
-  decode_mma_kernel<<<unsigned(grid), kThreads, kSmemBytes, stream>>>(p, kmap, vmap);
+  decode_mma_kernel<<<unsigned(grid), kThreads, kSmemBytes, stream>>>(p, kmap, vmap, kmap_half, vmap_half);
   return cudaGetLastError();
 }
 

@@ -38,9 +38,10 @@ struct DecodeParams {
 cudaError_t launch_decode(DecodeParams p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                           cudaStream_t stream);
 // tcgen05 decode (decode_mma.cu); cudaErrorNotSupported when it does not
-// cover the shape. Takes tensor maps with a {64, 1, 128} 128B-swizzled box.
+// cover the shape. Takes K/V tensor maps with a {64, 1, 128} 128B-swizzled
+// box and the same maps with a {64, 1, 64} box for short last tiles.
 cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
-                              cudaStream_t stream);
+                              const CUtensorMap& kmap_half, const CUtensorMap& vmap_half, cudaStream_t stream);
 int decode_group_chunk(int group);
 // Split-KV combine of lse_accum / out_accum into out (and lse).
 cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream);
