@@ -306,7 +306,7 @@ def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
             "workload": "config5: 4 seqs x ctx 32768, 64q/8kv, kv-head sharded over the GPUs, split-KV per GPU"}
 
 
-def engine_leg(nvb, dev, rank, world, runs=1):
+def engine_leg(nvb, dev, rank, world, runs=1, max_tokens=512):
     """the Qwen3-0.6B engine (28 layers, random weights
     N(0, 0.02)) generating for 256 requests with prompt ids uniform over the
     vocabulary, prompt lengths U[128, 1024], max_tokens 512, temperature 0.6
@@ -321,17 +321,19 @@ def engine_leg(nvb, dev, rank, world, runs=1):
 
     M, E = nvb.model, nvb.engine
     cfg = M.Qwen3Config()
-    n_req, lo, hi, max_tokens = 256, 128, 1024, 512
+    n_req, lo, hi, max_cap = 256, 128, 1024, 512
     g = torch.Generator().manual_seed(4000 + rank)
     lens = torch.randint(lo, hi + 1, (n_req,), generator=g).tolist()
     reqs = [E.Request(id=i, prompt_token_ids=torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist(),
                       max_tokens=max_tokens, temperature=0.6, ignore_eos=True) for i, n in enumerate(lens)]
     bs = 256
-    pages = sum(-(-(n + max_tokens) // bs) for n in lens)
-    sched = E.SchedulerConfig(block_size=bs, num_blocks=pages, max_sequences=n_req, max_model_len=hi + max_tokens,
+    # Capacities follow config 4 (max_tokens 512) even when a profiling run
+    # generates fewer tokens, so the decode geometry is the config's.
+    pages = sum(-(-(n + max_cap) // bs) for n in lens)
+    sched = E.SchedulerConfig(block_size=bs, num_blocks=pages, max_sequences=n_req, max_model_len=hi + max_cap,
                               max_batch_tokens=16384)
     opts = M.ModelOptions(device=dev.index or 0, block_size=bs, num_blocks=pages, max_batch_tokens=16384,
-                          max_sequences=n_req, max_model_len=hi + max_tokens, cuda_graphs=True)
+                          max_sequences=n_req, max_model_len=hi + max_cap, cuda_graphs=True)
     weights = M.random_weights(cfg, seed=0, device=dev)
     model = M.Qwen3Model(cfg, opts, weights)
     engine = E.LlmEngine(sched, model)
@@ -385,6 +387,8 @@ def main():
     ap.add_argument("--no-long-context", action="store_true")
     ap.add_argument("--no-engine", action="store_true")
     ap.add_argument("--engine-runs", type=int, default=1, help="timed generate() calls of the config-4 engine leg")
+    ap.add_argument("--engine-max-tokens", type=int, default=512,
+                    help="tokens per request in the engine leg (512 = config 4; fewer only for profiling runs)")
     ap.add_argument("--ref-budget", type=float, default=150.0,
                     help="seconds the reference arm's warm-up and timed steps may take in all")
     ap.add_argument("--batch", type=int, default=BATCH,
@@ -664,7 +668,7 @@ def main():
     # ---------------- config 4 engine, one replica per GPU
     engine = None
     if not args.no_engine:
-        engine = engine_leg(nvb, dev, rank, world, runs=args.engine_runs)
+        engine = engine_leg(nvb, dev, rank, world, runs=args.engine_runs, max_tokens=args.engine_max_tokens)
 
     # ---------------- CPU baseline (rank 0, N = 1 only)
     cpu = None
