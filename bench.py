@@ -279,20 +279,54 @@ def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
     for i in range(5):
         once(i)
     torch.cuda.synchronize()
+
+    # One CUDA graph per KV set: at N > 1 the whole step (decode, combine +
+    # peer stores, flag barrier) with its epoch in device memory, at N = 1 the
+    # decode and combine; the timed loop replays them in turn.
+    graphs = []
+    for c in cases:
+        if world > 1:
+            graphs.append(run.capture(c.q, c.k, c.v, c.cu_q, c.kv_lens, c.block_table))
+        else:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                run.local(c.q, c.k, c.v, c.cu_q, c.kv_lens, c.block_table, check=False)
+            graphs.append(g)
+
+    def replay(i):
+        if world > 1:
+            return run.replay(graphs[i % nsets])
+        graphs[i % nsets].replay()
+        return run.out_local
+
+    def timed(fn, n):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(n):
+            fn(i)
+        b.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / n], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    for i in range(5):
+        replay(i)
+    ms = timed(replay, steps)
+    # Untimed diagnostics of the same step (max over ranks): launched from the
+    # host without graphs, and the local decode + combine alone (no exchange).
+    breakdown = {"graph_ms": round(ms, 5), "eager_ms": round(timed(once, steps), 5)}
     if world > 1:
-        dist.barrier()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for i in range(steps):
-        once(i)
-    b.record(stream)
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
+        breakdown["local_decode_combine_ms"] = round(
+            timed(lambda i: run.local(cases[i % nsets].q, cases[i % nsets].k, cases[i % nsets].v,
+                                      cases[i % nsets].cu_q, cases[i % nsets].kv_lens, cases[i % nsets].block_table,
+                                      check=False), steps), 5)
     err = nvb.device_error()
+    del graphs
     run.close()  # every rank's GPU work is done (the all-reduce above)
     if err:
         raise RuntimeError(f"long-context decode recorded device error {err}")
@@ -300,7 +334,7 @@ def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
     return {"value": round(total_bytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 5),
             "splits_per_gpu": run.splits, "kv_heads_per_gpu": shard.kv_local,
             "l2": f"{nsets} KV sets of {set_bytes / 1e6:.0f} MB per GPU, used in turn",
-            "gather_check": check,
+            "gather_check": check, "breakdown": breakdown, "cuda_graph": True,
             "collective": ("combine fused with the all-gather: peer stores over NVLink + epoch-flag barrier "
                            "(nvb_paged_decode_gather)") if world > 1 else None,
             "workload": "config5: 4 seqs x ctx 32768, 64q/8kv, kv-head sharded over the GPUs, split-KV per GPU"}

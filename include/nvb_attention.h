@@ -129,6 +129,24 @@ int nvb_paged_decode_gather(void* stream, const void* q, const void* k, const vo
                             int num_splits, float* lse_accum, float* out_accum, void* const* peer_out,
                             unsigned int* const* peer_flag, int world, int rank, unsigned int epoch);
 
+/* The same step in a form that a CUDA graph can capture once and replay
+ * (no host argument changes between steps; no counterpart in the reference).
+ * The epoch lives in device memory: peer_flag[rank] needs world + 2 uint32
+ * (starting at 0): slot `world` is this rank's step counter, advanced at the
+ * end of each step, and slot world + 1 a count of finished combine CTAs (the
+ * last one runs the epoch exchange, so a step is two launches, decode and
+ * combine, and no separate barrier). Step n (n = 1, 2, ...)
+ * writes its results into output set n & 1: peer_out1[p] for odd n,
+ * peer_out0[p] for even n, each rank's [batch, world*q_heads, 128] BF16.
+ * Every rank must run the same number of steps in the same order; do not
+ * mix calls of this form and of nvb_paged_decode_gather on one flag set. */
+int nvb_paged_decode_gather_capturable(void* stream, const void* q, const void* k, const void* v, void* out_local,
+                                       const int* cu_q, const int* kv_lens, const int* block_table, int batch,
+                                       int max_k, int q_heads, int kv_heads, int block_size, int table_stride,
+                                       int num_blocks, int num_splits, float* lse_accum, float* out_accum,
+                                       void* const* peer_out0, void* const* peer_out1,
+                                       unsigned int* const* peer_flag, int world, int rank);
+
 /* Device buffers shared between the ranks of a node through CUDA IPC (the
  * outputs and flags of nvb_paged_decode_gather). create: cudaMalloc `bytes`
  * (zeroed) and write its 64-byte IPC handle; open: map a peer's handle;

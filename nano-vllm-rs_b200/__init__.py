@@ -48,6 +48,7 @@ def _declare(lib):
         "nvb_device_error": [ctypes.POINTER(c_int)],
         "nvb_clear_device_error": [],
         "nvb_paged_decode_gather": [_P] * 8 + [c_int] * 8 + [_P] * 4 + [c_int, c_int, ctypes.c_uint],
+        "nvb_paged_decode_gather_capturable": [_P] * 8 + [c_int] * 8 + [_P] * 5 + [c_int, c_int],
         "nvb_peer_buffer_create": [ctypes.c_size_t, ctypes.POINTER(c_void_p), _P],
         "nvb_peer_buffer_open": [_P, ctypes.POINTER(c_void_p)],
         "nvb_peer_buffer_close": [_P],
@@ -194,6 +195,39 @@ def paged_decode_gather(q, k, v, out_local, cu_q, kv_lens, block_table, *, batch
         _stream(stream), _ptr(q), _ptr(k), _ptr(v), _ptr(out_local), _ptr(cu_q), _ptr(kv_lens), _ptr(block_table),
         batch, max_k, q_heads, kv_heads, block_size, table_stride, num_blocks, num_splits, _ptr(lse_accum),
         _ptr(out_accum), ctypes.cast(outs, c_void_p), ctypes.cast(flags, c_void_p), world, rank, epoch))
+
+
+def paged_decode_gather_capturable(q, k, v, out_local, cu_q, kv_lens, block_table, *, batch, max_k, q_heads,
+                                   kv_heads, block_size, table_stride, num_blocks, num_splits, lse_accum, out_accum,
+                                   peer_out0, peer_out1, peer_flag, rank, stream=None, check=True):
+    """nvb_paged_decode_gather_capturable: the same step with the epoch kept
+    in device memory (slot len(peer_flag) of this rank's flags), so that a
+    CUDA graph can capture it once; step n writes output set n & 1
+    (`peer_out1` for odd n)."""
+    import torch
+
+    world = len(peer_out0)
+    if check:
+        _tensor(q, (batch, q_heads, 128), torch.bfloat16, "q")
+        _tensor(out_local, (batch, q_heads, 128), torch.bfloat16, "out_local")
+        for t, nm in ((k, "k"), (v, "v")):
+            _tensor(t, (num_blocks, block_size, kv_heads, 128), torch.bfloat16, nm)
+        _tensor(cu_q, (batch + 1,), torch.int32, "cu_q")
+        _tensor(kv_lens, (batch,), torch.int32, "kv_lens")
+        _tensor(block_table, (batch, table_stride), torch.int32, "block_table")
+        if num_splits > 1:
+            _tensor(lse_accum, (num_splits, batch, q_heads), torch.float32, "lse_accum")
+            _tensor(out_accum, (num_splits, batch, q_heads, 128), torch.float32, "out_accum")
+        if len(peer_out1) != world or len(peer_flag) != world or not 1 <= world <= 8:
+            raise ValueError("peer_out0, peer_out1 and peer_flag need one pointer per rank (1..8 ranks)")
+    o0 = (c_void_p * world)(*peer_out0)
+    o1 = (c_void_p * world)(*peer_out1)
+    flags = (c_void_p * world)(*peer_flag)
+    _check(library().nvb_paged_decode_gather_capturable(
+        _stream(stream), _ptr(q), _ptr(k), _ptr(v), _ptr(out_local), _ptr(cu_q), _ptr(kv_lens), _ptr(block_table),
+        batch, max_k, q_heads, kv_heads, block_size, table_stride, num_blocks, num_splits, _ptr(lse_accum),
+        _ptr(out_accum), ctypes.cast(o0, c_void_p), ctypes.cast(o1, c_void_p), ctypes.cast(flags, c_void_p), world,
+        rank))
 
 
 def paged_fwd(q, k, v, out, cu_q, kv_lens, block_table, *, batch, max_q, max_k, q_heads, kv_heads,

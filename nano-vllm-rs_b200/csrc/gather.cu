@@ -24,19 +24,53 @@ namespace gather_detail {
 constexpr int kMaxRanks = 8;
 
 struct PeerPtrs {
-  __nv_bfloat16* out[kMaxRanks];  // each rank's output [rows, qh_total, 128] for this step
-  unsigned int* flag[kMaxRanks];  // each rank's flags: slot p = last epoch rank p signalled there
+  __nv_bfloat16* out[2][kMaxRanks];  // two output sets, each rank's [rows, qh_total, 128]
+  unsigned int* flag[kMaxRanks];     // each rank's flags: slot p = last epoch rank p signalled there
 };
+
+// Epoch of the step being run: the host's, or (counter != null) one past the
+// rank's device counter, which the barrier kernel advances at the end of the
+// step. The step's results go to output set `epoch & 1` in the counter form.
+__device__ __forceinline__ unsigned int step_epoch(unsigned int host_epoch, const unsigned int* counter) {
+  return counter ? *counter + 1u : host_epoch;
+}
+
+// Lanes p < world: signal `epoch` into rank p's slot `rank`, then wait (bounded)
+// until rank p's epoch has arrived in this rank's slot p.
+__device__ __forceinline__ void exchange_epoch(const PeerPtrs& peers, int world, int rank, unsigned int epoch,
+                                               int lane) {
+  if (lane >= world) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.flag[lane] + rank), "r"(epoch) : "memory");
+  const unsigned int* mine = peers.flag[rank] + lane;
+  const long long start = clock64();
+  for (;;) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+    if (int(v - epoch) >= 0) break;  // epochs only grow (wrap-safe)
+    if (clock64() - start > kWaitCycles) {
+      record_error(kErrGatherWait);
+      break;
+    }
+    __nanosleep(100);
+  }
+}
 
 // One warp per (row, local head). splits > 1: weights split s by
 // exp(lse_s - max lse) like combine_kernel (decode.cu); splits == 1: copies
 // the local decode output. The result goes to every rank at head offset
 // head_offset (= rank * qh local).
+// kBarrier (the counter form): the CTA that finishes last (a done count in
+// the rank's flag slot world + 1; every CTA fences its peer stores at system
+// scope before counting) runs the epoch exchange itself, advances the device
+// epoch and resets the count, so the step needs no separate barrier launch.
+template <bool kBarrier>
 __global__ void __launch_bounds__(256) combine_gather_kernel(const float* __restrict__ lse_accum,
                                                              const float* __restrict__ out_accum,
                                                              const __nv_bfloat16* __restrict__ local_out, int rows,
                                                              int qh, int splits, PeerPtrs peers, int world,
-                                                             int head_offset, int qh_total) {
+                                                             int head_offset, int qh_total, unsigned int* counter,
+                                                             int rank) {
   // Launched as a programmatic dependent of the decode grid (see
   // nvb_paged_decode_gather): the barrier kernel after it may be scheduled
   // now, and this grid waits for the decode to complete before reading.
@@ -44,7 +78,7 @@ __global__ void __launch_bounds__(256) combine_gather_kernel(const float* __rest
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (item >= (long long)rows * qh) return;
+  if (item < (long long)rows * qh) {
   uint2 packed;
   if (splits > 1) {
     const long long stride = (long long)rows * qh;
@@ -75,33 +109,41 @@ __global__ void __launch_bounds__(256) combine_gather_kernel(const float* __rest
   }
   const long long row = item / qh, h = item - row * qh;
   const long long dst = (row * qh_total + head_offset + h) * 128 + lane * 4;
-  for (int p = 0; p < world; ++p) *reinterpret_cast<uint2*>(peers.out[p] + dst) = packed;
+  const int set = counter ? int(step_epoch(0, counter) & 1u) : 0;
+  for (int p = 0; p < world; ++p) *reinterpret_cast<uint2*>(peers.out[set][p] + dst) = packed;
+  }
   __threadfence_system();  // the stores are visible to the peers before this thread ends
+  if constexpr (kBarrier) {
+    __shared__ int last;
+    __syncthreads();
+    unsigned int* done = counter + 1;
+    if (threadIdx.x == 0) last = atomicAdd(done, 1u) == unsigned(gridDim.x) - 1u;
+    __syncthreads();
+    if (!last || threadIdx.x >= 32) return;
+    __threadfence_system();
+    const unsigned int epoch = step_epoch(0, counter);
+    exchange_epoch(peers, world, rank, epoch, lane);
+    __syncwarp();
+    if (lane == 0) {
+      *done = 0u;
+      *counter = epoch;
+    }
+  }
 }
 
 // One warp: lane p writes this rank's epoch into rank p's flag slot `rank`,
-// then waits until rank p's epoch has arrived in this rank's slot p.
-__global__ void gather_barrier_kernel(PeerPtrs peers, int world, int rank, unsigned int epoch) {
+// then waits until rank p's epoch has arrived in this rank's slot p. In the
+// counter form lane 0 then advances the device counter to this epoch.
+__global__ void gather_barrier_kernel(PeerPtrs peers, int world, int rank, unsigned int host_epoch,
+                                      unsigned int* counter) {
   // Every store of the combine grid before it is complete and visible before
   // this rank signals its peers (programmatic dependent launch).
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x;
-  if (lane < world) {
-    __threadfence_system();
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.flag[lane] + rank), "r"(epoch) : "memory");
-    const unsigned int* mine = peers.flag[rank] + lane;
-    const long long start = clock64();
-    for (;;) {
-      unsigned int v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
-      if (int(v - epoch) >= 0) break;  // epochs only grow (wrap-safe)
-      if (clock64() - start > kWaitCycles) {
-        record_error(kErrGatherWait);
-        break;
-      }
-      __nanosleep(100);
-    }
-  }
+  const unsigned int epoch = step_epoch(host_epoch, counter);
+  exchange_epoch(peers, world, rank, epoch, lane);
+  __syncwarp();
+  if (counter && lane == 0) *counter = epoch;
 }
 
 }  // namespace gather_detail
@@ -151,27 +193,32 @@ extern "C" int nvb_peer_buffer_free(void* ptr) {
   return cuda_status(cudaFree(ptr), "cudaFree(peer buffer)");
 }
 
-extern "C" int nvb_paged_decode_gather(void* stream, const void* q, const void* k, const void* v, void* out_local,
-                                       const int* cu_q, const int* kv_lens, const int* block_table, int batch,
-                                       int max_k, int q_heads, int kv_heads, int block_size, int table_stride,
-                                       int num_blocks, int num_splits, float* lse_accum, float* out_accum,
-                                       void* const* peer_out, unsigned int* const* peer_flag, int world, int rank,
-                                       unsigned int epoch) {
-  using namespace nvb;
+namespace nvb {
+namespace gather_detail {
+
+int gather_impl(void* stream, const void* q, const void* k, const void* v, void* out_local, const int* cu_q,
+                const int* kv_lens, const int* block_table, int batch, int max_k, int q_heads, int kv_heads,
+                int block_size, int table_stride, int num_blocks, int num_splits, float* lse_accum, float* out_accum,
+                void* const* out0, void* const* out1, unsigned int* const* peer_flag, int world, int rank,
+                unsigned int epoch) {
   using namespace nvb::api_detail;
-  using namespace nvb::gather_detail;
   g_last_error[0] = 0;
-  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !peer_out || !peer_flag || batch <= 0 ||
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !out0 || !peer_flag || batch <= 0 ||
       q_heads <= 0)
     return fail("invalid gather arguments (world 1..%d, rank in [0, world))", kMaxRanks);
   PeerPtrs peers{};
   for (int p = 0; p < world; ++p) {
-    if (!peer_out[p] || !peer_flag[p] || (reinterpret_cast<uintptr_t>(peer_out[p]) & 15) ||
-        (reinterpret_cast<uintptr_t>(peer_flag[p]) & 3))
-      return fail("peer %d: output must be 16-byte aligned and flags 4-byte aligned", p);
-    peers.out[p] = static_cast<__nv_bfloat16*>(peer_out[p]);
+    for (int set = 0; set < (out1 ? 2 : 1); ++set) {
+      void* o = set ? out1[p] : out0[p];
+      if (!o || (reinterpret_cast<uintptr_t>(o) & 15))
+        return fail("peer %d: outputs must be non-null and 16-byte aligned", p);
+      peers.out[set][p] = static_cast<__nv_bfloat16*>(o);
+    }
+    if (!peer_flag[p] || (reinterpret_cast<uintptr_t>(peer_flag[p]) & 3))
+      return fail("peer %d: flags must be non-null and 4-byte aligned", p);
     peers.flag[p] = peer_flag[p];
   }
+  unsigned int* counter = out1 ? peer_flag[rank] + world : nullptr;
   const bool partials = num_splits > 1 && block_size % 128 == 0;
   const int rc = paged_fwd_impl(stream, q, k, v, out_local, cu_q, kv_lens, block_table, batch, batch, 1, max_k,
                                 q_heads, kv_heads, block_size, table_stride, num_splits, nullptr, lse_accum,
@@ -191,14 +238,55 @@ extern "C" int nvb_paged_decode_gather(void* stream, const void* q, const void* 
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, combine_gather_kernel, static_cast<const float*>(lse_accum),
+  if (counter) {
+    // Counter form: the combine's last CTA runs the epoch exchange.
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, combine_gather_kernel<true>, static_cast<const float*>(lse_accum),
+                                             static_cast<const float*>(out_accum),
+                                             static_cast<const __nv_bfloat16*>(out_local), batch, q_heads,
+                                             partials ? num_splits : 1, peers, world, rank * q_heads,
+                                             world * q_heads, counter, rank);
+    return cuda_status(e, "gather launch");
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, combine_gather_kernel<false>, static_cast<const float*>(lse_accum),
                                      static_cast<const float*>(out_accum),
                                      static_cast<const __nv_bfloat16*>(out_local), batch, q_heads,
-                                     partials ? num_splits : 1, peers, world, rank * q_heads, world * q_heads);
+                                     partials ? num_splits : 1, peers, world, rank * q_heads, world * q_heads,
+                                     counter, rank);
   if (e == cudaSuccess) {
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(32);
-    e = cudaLaunchKernelEx(&cfg, gather_barrier_kernel, peers, world, rank, epoch);
+    e = cudaLaunchKernelEx(&cfg, gather_barrier_kernel, peers, world, rank, epoch, counter);
   }
   return cuda_status(e, "gather launch");
+}
+
+}  // namespace gather_detail
+}  // namespace nvb
+
+extern "C" int nvb_paged_decode_gather(void* stream, const void* q, const void* k, const void* v, void* out_local,
+                                       const int* cu_q, const int* kv_lens, const int* block_table, int batch,
+                                       int max_k, int q_heads, int kv_heads, int block_size, int table_stride,
+                                       int num_blocks, int num_splits, float* lse_accum, float* out_accum,
+                                       void* const* peer_out, unsigned int* const* peer_flag, int world, int rank,
+                                       unsigned int epoch) {
+  return nvb::gather_detail::gather_impl(stream, q, k, v, out_local, cu_q, kv_lens, block_table, batch, max_k,
+                                         q_heads, kv_heads, block_size, table_stride, num_blocks, num_splits,
+                                         lse_accum, out_accum, peer_out, nullptr, peer_flag, world, rank, epoch);
+}
+
+extern "C" int nvb_paged_decode_gather_capturable(void* stream, const void* q, const void* k, const void* v,
+                                                  void* out_local, const int* cu_q, const int* kv_lens,
+                                                  const int* block_table, int batch, int max_k, int q_heads,
+                                                  int kv_heads, int block_size, int table_stride, int num_blocks,
+                                                  int num_splits, float* lse_accum, float* out_accum,
+                                                  void* const* peer_out0, void* const* peer_out1,
+                                                  unsigned int* const* peer_flag, int world, int rank) {
+  using namespace nvb::api_detail;
+  if (!peer_out1) {
+    g_last_error[0] = 0;
+    return fail("the capturable gather needs two output sets");
+  }
+  return nvb::gather_detail::gather_impl(stream, q, k, v, out_local, cu_q, kv_lens, block_table, batch, max_k,
+                                         q_heads, kv_heads, block_size, table_stride, num_blocks, num_splits,
+                                         lse_accum, out_accum, peer_out0, peer_out1, peer_flag, world, rank, 0u);
 }

@@ -13,8 +13,10 @@ Two partitions of the work, one process per GPU over torch.distributed:
   batch * q_heads * 256 B (8 KiB per rank at 4 x 64 heads), so a separate
   collective is launch-latency bound. The default (`fused=True`) stores each
   combined result straight into every rank's output from the combine kernel
-  (peer stores over NVLink into CUDA IPC buffers, then an epoch-flag barrier:
-  nvb_paged_decode_gather); `fused=False` keeps the NCCL all-gather.
+  (peer stores over NVLink into CUDA IPC buffers, then an epoch-flag barrier
+  whose epoch lives in device memory: nvb_paged_decode_gather_capturable), so
+  a whole step can be captured in a CUDA graph once and replayed;
+  `fused=False` keeps the NCCL all-gather.
 
 The reference is single-GPU (its README: no NCCL, MPI or tensor
 parallelism); this module is the B200 build's own.
@@ -100,7 +102,9 @@ class KvHeadShardedDecode:
     [batch, q_local, 128] (the query heads of this rank's kv heads).
     fused=True (default): combine and all-gather in one kernel through peer
     memory; the returned tensor is one of two output buffers used in turn
-    and stays valid until the call after next. fused=False: NCCL all-gather.
+    and stays valid until the call after next. `capture` records one such
+    step in a CUDA graph and `replay` runs it (every rank must call and
+    replay in the same order). fused=False: NCCL all-gather.
     Call close() before destroying the process group."""
 
     FLAG_BYTES = 256
@@ -162,13 +166,35 @@ class KvHeadShardedDecode:
         if not self.fused:
             self.local(q_local, k_local, v_local, cu_q, kv_lens, block_table, check)
             return gather_heads(self.out_local, self.shard, self.group)
+        self._fused_step(q_local, k_local, v_local, cu_q, kv_lens, block_table, check)
         self.epoch += 1
-        i = self.epoch & 1
-        self.nvb.paged_decode_gather(q_local, k_local, v_local, self.out_local, cu_q, kv_lens, block_table,
-                                     batch=self.batch, max_k=self.max_k, q_heads=self.shard.q_local,
-                                     kv_heads=self.shard.kv_local, block_size=self.block_size,
-                                     table_stride=self.table_stride, num_blocks=self.num_blocks,
-                                     num_splits=self.splits, lse_accum=self.la, out_accum=self.oa,
-                                     peer_out=self.out_ptrs[i], peer_flag=self.flag_ptrs, rank=self.shard.rank,
-                                     epoch=self.epoch, check=check)
-        return self.views[i]
+        return self.views[self.epoch & 1]
+
+    def _fused_step(self, q_local, k_local, v_local, cu_q, kv_lens, block_table, check):
+        # The step's epoch is the device counter + 1 (advanced by the step
+        # itself); self.epoch mirrors it on the host to name the output set.
+        self.nvb.paged_decode_gather_capturable(
+            q_local, k_local, v_local, self.out_local, cu_q, kv_lens, block_table, batch=self.batch,
+            max_k=self.max_k, q_heads=self.shard.q_local, kv_heads=self.shard.kv_local, block_size=self.block_size,
+            table_stride=self.table_stride, num_blocks=self.num_blocks, num_splits=self.splits, lse_accum=self.la,
+            out_accum=self.oa, peer_out0=self.out_ptrs[0], peer_out1=self.out_ptrs[1], peer_flag=self.flag_ptrs,
+            rank=self.shard.rank, check=check)
+
+    def capture(self, q_local, k_local, v_local, cu_q, kv_lens, block_table):
+        """A CUDA graph of one fused step on these inputs (nothing runs while
+        capturing). Call the step eagerly once before, so the library has
+        set up its kernels and descriptors."""
+        import torch
+
+        if not self.fused:
+            raise ValueError("capture needs the fused gather")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self._fused_step(q_local, k_local, v_local, cu_q, kv_lens, block_table, True)
+        return graph
+
+    def replay(self, graph):
+        """Runs a captured step; returns this step's output set."""
+        graph.replay()
+        self.epoch += 1
+        return self.views[self.epoch & 1]

@@ -58,6 +58,43 @@ def test_gather_world1_matches_paged_fwd(nvb, splits):
         nvb.peer_buffer_free(ptr)
 
 
+@pytest.mark.parametrize("splits", [1, 6])
+def test_capturable_gather_world1_graph_replay(nvb, splits):
+    """The capturable form: eager steps, then one captured step replayed
+    three times; the device epoch picks the output set (odd steps set 1),
+    and every step matches nvb_paged_fwd."""
+    import importlib
+
+    S = importlib.import_module("nano_vllm_rs_b200.sharding")
+    case = nvb.workloads.paged_case([3000, 1200, 5000], q_heads=32, kv_heads=8, seed=32)
+    ref = _reference(nvb, case, splits)
+    shard = S.HeadShard(0, 1, kv_heads=8, q_heads=32)
+    run = S.KvHeadShardedDecode(nvb, shard, batch=case.batch, block_size=case.block_size,
+                                table_stride=case.table_stride, num_blocks=case.num_blocks,
+                                max_k=int(case.kv_lens.max()), device=torch.device("cuda"), num_splits=splits)
+    try:
+        seen = []
+        for step in range(1, 3):
+            got = run(case.q, case.k, case.v, case.cu_q, case.kv_lens, case.block_table)
+            torch.cuda.synchronize()
+            assert got.data_ptr() == run.views[step & 1].data_ptr()
+            assert_close(as_f32(got), as_f32(ref), 2e-2, 2e-3, what=f"eager step {step}")
+            seen.append(got.data_ptr())
+        graph = run.capture(case.q, case.k, case.v, case.cu_q, case.kv_lens, case.block_table)
+        for step in range(3, 6):
+            run.views[step & 1].zero_()
+            got = run.replay(graph)
+            torch.cuda.synchronize()
+            assert got.data_ptr() == run.views[step & 1].data_ptr()
+            assert_close(as_f32(got), as_f32(ref), 2e-2, 2e-3, what=f"replayed step {step}")
+        assert nvb.device_error() == 0
+        counter = torch.as_tensor(S._DeviceArray(run.flag_ptrs[0] + 4, (1,), "<i4"), device="cuda")
+        assert int(counter.item()) == 5  # slot `world` of the flags: the device epoch
+        del graph
+    finally:
+        run.close()
+
+
 def test_gather_rejects_bad_arguments(nvb):
     case = nvb.workloads.paged_case([300], q_heads=16, kv_heads=8, seed=2)
     local = torch.empty_like(case.q)
@@ -111,6 +148,12 @@ def _two_gpu_worker(rank, world, port, q):
             got = run(q_l, k_l, v_l, full.cu_q, full.kv_lens, full.block_table)
             torch.cuda.synchronize()
             errs.append(float((got.float().cpu() - ref).abs().max()))
+        graph = run.capture(q_l, k_l, v_l, full.cu_q, full.kv_lens, full.block_table)
+        for _ in range(3):  # the same step replayed from a CUDA graph
+            got = run.replay(graph)
+            torch.cuda.synchronize()
+            errs.append(float((got.float().cpu() - ref).abs().max()))
+        del graph
         dev_err = nvb.device_error()
         dist.barrier()
         run.close()
