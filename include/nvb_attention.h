@@ -57,8 +57,8 @@ extern "C" {
  *    + i] for query i of sequence b.
  *
  * Limits: head_dim 128, block_size a positive multiple of 256, q_heads a
- * multiple of kv_heads with at most 16 query heads per kv head, q_heads <=
- * 256, 1 <= num_splits <= 128. Unlike the reference (max_k <= 4096) the
+ * multiple of kv_heads, q_heads <= 256 (any GQA group, as the reference:
+ * flash_native.cu:48-52), 1 <= num_splits <= 128. Unlike the reference (max_k <= 4096) the
  * context is bounded only by block_size * table_stride < 2^31.
  * Like the reference, page ids are trusted: a negative page id masks its
  * tokens, a page id past the end of the cache is undefined behaviour. Use

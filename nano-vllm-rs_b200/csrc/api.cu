@@ -204,13 +204,13 @@ int run_decode(cudaStream_t stream, DecodeParams p, const void* k, const void* v
   const long long tokens = (long long)p.num_blocks * p.block_size;
   CUtensorMap kmap, vmap;
   p.scale_log2 = kScaleLog2;
-  if (p.mode == kModeDecode && p.block_size % 128 == 0 && p.qh / p.kvh <= 16) {
+  if (p.mode == kModeDecode && p.block_size % 128 == 0) {
     if (int rc = kv_mma_map(k, tokens, p.kvh, &kmap)) return rc;
     if (int rc = kv_mma_map(v, tokens, p.kvh, &vmap)) return rc;
     CUtensorMap khalf, vhalf;
     if (int rc = kv_mma_map(k, tokens, p.kvh, &khalf, 64)) return rc;
     if (int rc = kv_mma_map(v, tokens, p.kvh, &vhalf, 64)) return rc;
-    p.n_hgroups = 1;
+    p.n_hgroups = (p.qh / p.kvh + 15) / 16;
     cudaError_t e = launch_decode_mma(p, kmap, vmap, khalf, vhalf, stream);
     if (e != cudaErrorNotSupported) {
       if (e == cudaSuccess && p.num_splits > 1 && combine) e = launch_combine(p, stream);
@@ -240,7 +240,6 @@ int paged_fwd_impl(void* stream, const void* q, const void* k, const void* v, vo
       num_splits < 1 || num_splits > 128 || (max_q == 1 && total_q != batch) || (max_q != 1 && num_splits != 1) ||
       (num_splits > 1 && (!lse_accum || !out_accum)))
     return fail("invalid paged attention BF16 hdim128 arguments");
-  if (q_heads / kv_heads > 16) return fail("at most 16 query heads per kv head are supported");
   if (bounded && (num_blocks <= 0 || (long long)num_blocks * block_size > INT_MAX))
     return fail("num_blocks must be positive and num_blocks * block_size must fit in int32");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || (out_accum && !aligned16(out_accum)))
@@ -319,7 +318,6 @@ int native_impl(void* stream, const void* q, const void* kc, const void* vc, con
   }
   if (bs % 32) return fail("block_size must be a multiple of 32 (got %d)", bs);
   if ((long long)blocks * bs > INT_MAX) return fail("num_blocks * block_size must fit in int32");
-  if (qh / kvh > 16) return fail("at most 16 query heads per kv head are supported");
   if (partitions < 1 || partitions > 128 || (partitions > 1 && !scratch))
     return fail("partitions must be in [1, 128] with scratch for more than one");
   if (!aligned16(q) || !aligned16(kc) || !aligned16(vc) || !aligned16(out) || (scratch && !aligned16(scratch)))
@@ -385,7 +383,10 @@ int nvb_num_splits(int batch, int q_heads, int kv_heads, int max_k, int num_sms)
   int group = q_heads / kv_heads, gc = 1;
   for (int c = 8; c >= 1; --c)
     if (group % c == 0) { gc = c; break; }
-  const long long work = (long long)batch * kv_heads * (group / gc);
+  // CTAs per (sequence, kv head): 16-head groups in the tensor-core decode
+  // past 16 heads, the CUDA-core decode's head chunks below.
+  const long long units = group > 16 ? (group + 15) / 16 : group / gc;
+  const long long work = (long long)batch * kv_heads * units;
   const long long target = 2LL * num_sms;  // two resident CTAs per SM
   if (work >= target) return 1;
   // The most splits that still fit one wave of resident CTAs: a split count

@@ -5,7 +5,9 @@
 // kernels/kernels.cu:288-354 and the FA2 decode behind
 // kernels/flash_native/flash_native.cu:61-112); this kernel moves both
 // contractions onto the tensor cores with the KV tokens as the M dimension,
-// so the GQA group (<= 16 query heads) fits the N = 16 of one MMA:
+// so up to 16 query heads of a GQA group fit the N = 16 of one MMA (larger
+// groups run as several 16-head CTAs per kv head, adjacent in the grid so
+// they read each K/V tile while it is in L2):
 //
 //   S^T_j = K_j Q^T      M = 128 tokens, N = 16 heads, K = 128 dims
 //                        A = K tile (K-major, 128B-swizzled smem, by TMA)
@@ -142,10 +144,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   int cta = blockIdx.x;
   const int split = cta % p.num_splits;
   cta /= p.num_splits;
+  const int hgroup = cta % p.n_hgroups;
+  cta /= p.n_hgroups;
   const int kvhead = cta % p.kvh;
   const int row = cta / p.kvh;
-  const int group = p.qh / p.kvh;  // <= kN
-  const int head0 = kvhead * group;
+  const int head0 = kvhead * (p.qh / p.kvh) + hgroup * kN;
+  const int group = min(kN, p.qh / p.kvh - hgroup * kN);  // this CTA's heads
   const int len = p.lens[row];
   const bool valid = len >= 1 && (long long)len <= (long long)p.table_stride * p.block_size;
   const int n_tiles_total = valid ? (len + kTok - 1) / kTok : 0;
@@ -471,13 +475,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 }  // namespace decode_mma_detail
 
-// Returns cudaErrorNotSupported for shapes this kernel does not cover
-// (groups above 16 query heads, pages that are not a multiple of 128 tokens).
+// Returns cudaErrorNotSupported for shapes this kernel does not cover (pages
+// that are not a multiple of 128 tokens). p.n_hgroups must be
+// ceil(group / 16).
 cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                               const CUtensorMap& kmap_half, const CUtensorMap& vmap_half, cudaStream_t stream) {
   using namespace decode_mma_detail;
   const int group = p.qh / p.kvh;
-  if (p.mode != kModeDecode || group > kN || p.block_size % kTok) return cudaErrorNotSupported;
+  if (p.mode != kModeDecode || p.block_size % kTok || p.n_hgroups != (group + kN - 1) / kN)
+    return cudaErrorNotSupported;
   static unsigned configured[kContextSlots] = {};
   const cudaError_t e = once_per_context(configured, [] {
     cudaError_t r = cudaFuncSetAttribute(decode_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
@@ -486,7 +492,7 @@ cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& kmap, co
                                 cudaSharedmemCarveoutMaxShared);
   });
   if (e != cudaSuccess) return e;
-  const long long grid = (long long)p.rows * p.kvh * p.num_splits;
+  const long long grid = (long long)p.rows * p.kvh * p.n_hgroups * p.num_splits;
   if (grid <= 0 || grid > 0x7fffffffLL) return cudaErrorInvalidValue;
   decode_mma_kernel<<<unsigned(grid), kThreads, kSmemBytes, stream>>>(p, kmap, vmap, kmap_half, vmap_half);
   return cudaGetLastError();

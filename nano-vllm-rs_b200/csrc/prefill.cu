@@ -821,7 +821,9 @@ int* sched_pair(cudaStream_t stream, cudaError_t* err) {
 cudaError_t launch_prefill(const PrefillArgs& a, cudaStream_t stream) {
   using namespace prefill_detail;
   const int group = a.qh / a.kvh;
-  if (group < 1 || group > 16 || a.batch > 65535 || a.kvh > 65535) return cudaErrorNotSupported;
+  // Up to 128 query heads per kv head: a 128-row query tile holds 128 / group
+  // queries of the group (at least one).
+  if (group < 1 || group > kRows || a.batch > 65535 || a.kvh > 65535) return cudaErrorNotSupported;
   const int qt = kRows / group;
   // Every sequence within one query tile (chunked prefill of short chunks):
   // tile B of every pair would be empty, so one tile per item runs faster.
