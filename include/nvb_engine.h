@@ -145,6 +145,12 @@ typedef struct NvbeModelOptions {
   int max_sequences;
   int max_model_len;
   int cuda_graphs;
+  /* 1: projections of small forwards (decode steps of up to 16 sequences,
+   * and up to 64 for projections of at most 2048 outputs, where it was
+   * measured faster) run on this library's tcgen05 GEMM (nvbe_layer_gemm,
+   * SiLU fused into the gate/up projection); larger ones and the LM head use
+   * cuBLAS. 0: cuBLAS throughout. */
+  int tc_gemms;
 } NvbeModelOptions;
 
 /* Borrowed BF16 device weights, row-major [out, in] like the checkpoint
@@ -212,6 +218,24 @@ int nvbe_layer_silu_mul(void* stream, const void* packed, void* out, int rows, i
 /* nv_gather: out[r] = x[indices[r]] (zero for indices outside [0, input_rows)). */
 int nvbe_layer_gather(void* stream, const void* x, const int* indices, void* out, int rows, int hidden,
                       int input_rows);
+/* Decode-shaped GEMM on tcgen05 tensor cores, replacing the reference's
+ * cublasGemmEx for M <= 256 rows (kernels/kernels.cu:98-106):
+ * y[M, N] = x[M, K] w[N, K]^T, BF16 in and out, FP32 accumulation, K split
+ * over a thread-block cluster and summed in a fixed order (deterministic).
+ * silu = 1: w holds gate rows then up rows ([2I, K], N = 2I) and
+ * y[M, I] = silu(gate) * up with the reference's SiLU arithmetic on the
+ * BF16-rounded gate and up (kernels/kernels.cu:355-364). K a multiple of
+ * 64, N a multiple of 4 (8 with silu), pointers 16-byte aligned. The FP32
+ * split-K partials go through `workspace` (at least
+ * nvbe_gemm_workspace_bytes(M, N, K, silu) bytes; the call allocates
+ * nothing). */
+size_t nvbe_gemm_workspace_bytes(int M, int N, int K, int silu);
+int nvbe_layer_gemm(void* stream, const void* x, const void* w, void* y, int M, int N, int K, int silu,
+                    void* workspace, size_t workspace_bytes);
+/* The decode GEMM's device error word: 0, or 1 when a pipeline wait gave up
+ * (about two seconds); -1 if it cannot be read. */
+int nvbe_gemm_device_error(void);
+
 /* nv_sample_parallel: Gumbel-max sampling with the reference's SplitMix64
  * stream (temperature 0: argmax), ties to the lowest token id. The partial
  * buffers hold rows * nvbe_sample_partitions(vocab) entries each. */

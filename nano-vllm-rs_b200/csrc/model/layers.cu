@@ -101,6 +101,10 @@ __global__ void __launch_bounds__(128) rms_row_kernel(const __nv_bfloat16* __res
                                                       __nv_bfloat16* __restrict__ residual,
                                                       const __nv_bfloat16* __restrict__ weight,
                                                       __nv_bfloat16* __restrict__ out, int hidden, float eps) {
+  // A decode GEMM launched after this kernel as a programmatic dependent may
+  // start streaming its weights now; it waits for this grid before reading
+  // the normed rows.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const long long base = (long long)blockIdx.x * hidden;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float v[2][NV];

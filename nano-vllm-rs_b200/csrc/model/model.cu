@@ -22,6 +22,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -99,6 +100,11 @@ struct NvbeModel {
   cublasHandle_t blas = nullptr;
   std::unordered_map<int, cudaGraphExec_t> graphs;
   size_t last_samples = 0;
+  // tcgen05 decode GEMMs: weight maps per layer, input maps per row count.
+  std::vector<CUtensorMap> map_qkv, map_o, map_gate_up, map_down;
+  std::unordered_map<int, CUtensorMap> map_in[3];  // normed, attention, activated; keyed by rows
+  void* gemm_ws = nullptr;  // split-K partials of the decode GEMMs
+  size_t gemm_ws_bytes = 0;
 
   int alloc(void** p, size_t bytes, const char* what) {
     TRY(cuda_rc(cudaMalloc(p, bytes), what));
@@ -106,6 +112,7 @@ struct NvbeModel {
     return cuda_rc(cudaMemsetAsync(*p, 0, bytes, stream), what);
   }
   int gemm(const void* x, const void* w, void* y, int m, int n, int k);
+  int tc_gemm(int which, const CUtensorMap& wmap, void* y, int m, int n, int k, bool silu);
   int forward(int rows, int sequences, int samples, int max_q, int max_k);
   void release();
 };
@@ -117,6 +124,21 @@ int NvbeModel::gemm(const void* x, const void* w, void* y, int m, int n, int k) 
   return blas_rc(cublasGemmEx(blas, CUBLAS_OP_T, CUBLAS_OP_N, n, m, k, &alpha, w, CUDA_R_16BF, k, x, CUDA_R_16BF, k,
                               &beta, y, CUDA_R_16BF, n, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT),
                  "cublasGemmEx");
+}
+
+// The decode GEMM from input buffer `which` (0 normed, 1 attention, 2
+// activated) with `m` rows; the input map is built once per row count.
+int NvbeModel::tc_gemm(int which, const CUtensorMap& wmap, void* y, int m, int n, int k, bool silu) {
+  auto it = map_in[which].find(m);
+  if (it == map_in[which].end()) {
+    const void* x = which == 0 ? normed : which == 1 ? attention : activated;
+    CUtensorMap map;
+    if (nvbm::gemm_input_map(x, m, k, &map)) return mfail("decode GEMM input map (rows %d, K %d)", m, k);
+    it = map_in[which].emplace(m, map).first;
+  }
+  return cuda_rc(nvbm::launch_gemm_decode(stream, wmap, it->second, y, m, n, k, silu ? n / 2 : n, silu, sms, gemm_ws,
+                                          gemm_ws_bytes),
+                 "decode GEMM launch");
 }
 
 void NvbeModel::release() {
@@ -141,6 +163,8 @@ int NvbeModel::forward(int rows, int sequences, int nsamples, int max_q, int max
   const int q_size = qh * D, qkv_size = q_size + 2 * kvh * D, I = c.intermediate_size;
   TRY(cuda_rc(nvbm::launch_embedding(stream, tokens, embedding, residual, rows, H, c.vocab_size, sms), "embedding"));
   const int splits = max_q == 1 ? decode_splits[size_t(sequences)] : 1;
+  // tcgen05 decode GEMMs where they beat cuBLAS (small batches); cuBLAS else.
+  auto tc = [&](int n, int k) { return o.tc_gemms && nvbm::gemm_decode_preferred(rows, n, k); };
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     if (l == 0)
       TRY(cuda_rc(nvbm::launch_rms(stream, residual, nullptr, input_norm[l], normed, rows, H, c.rms_norm_eps),
@@ -148,7 +172,10 @@ int NvbeModel::forward(int rows, int sequences, int nsamples, int max_q, int max
     else
       TRY(cuda_rc(nvbm::launch_rms(stream, hidden, residual, input_norm[l], normed, rows, H, c.rms_norm_eps),
                   "add_rms_norm"));
-    TRY(gemm(normed, qkv_w[l], qkv, rows, qkv_size, H));
+    if (tc(qkv_size, H))
+      TRY(tc_gemm(0, map_qkv[size_t(l)], qkv, rows, qkv_size, H, false));
+    else
+      TRY(gemm(normed, qkv_w[l], qkv, rows, qkv_size, H));
     TRY(nvb_rc(nvb_qkv_rope_cached(stream, qkv, q_norm[l], k_norm[l], positions, slots, query, k_cache[l],
                                    v_cache[l], rows, qh, kvh, D, o.block_size, o.num_blocks, c.rms_norm_eps, rope,
                                    o.max_model_len),
@@ -157,12 +184,23 @@ int NvbeModel::forward(int rows, int sequences, int nsamples, int max_q, int max
                                 rows, max_q, max_k, qh, kvh, o.block_size, table_stride, splits, nullptr,
                                 splits > 1 ? lse_accum : nullptr, splits > 1 ? out_accum : nullptr, o.num_blocks),
                "nvb_paged_fwd_ex"));
-    TRY(gemm(attention, o_proj[l], hidden, rows, H, q_size));
+    if (tc(H, q_size))
+      TRY(tc_gemm(1, map_o[size_t(l)], hidden, rows, H, q_size, false));
+    else
+      TRY(gemm(attention, o_proj[l], hidden, rows, H, q_size));
     TRY(cuda_rc(nvbm::launch_rms(stream, hidden, residual, post_norm[l], normed, rows, H, c.rms_norm_eps),
                 "add_rms_norm"));
-    TRY(gemm(normed, gate_up_w[l], gate_up, rows, 2 * I, H));
-    TRY(cuda_rc(nvbm::launch_silu_mul(stream, gate_up, activated, rows, I, sms), "silu_mul"));
-    TRY(gemm(activated, down_w[l], hidden, rows, H, I));
+    if (tc(2 * I, H)) {
+      // gate/up projection with SiLU * up fused into its epilogue
+      TRY(tc_gemm(0, map_gate_up[size_t(l)], activated, rows, 2 * I, H, true));
+    } else {
+      TRY(gemm(normed, gate_up_w[l], gate_up, rows, 2 * I, H));
+      TRY(cuda_rc(nvbm::launch_silu_mul(stream, gate_up, activated, rows, I, sms), "silu_mul"));
+    }
+    if (tc(H, I))
+      TRY(tc_gemm(2, map_down[size_t(l)], hidden, rows, H, I, false));
+    else
+      TRY(gemm(activated, down_w[l], hidden, rows, H, I));
   }
   if (nsamples > 0) {
     TRY(cuda_rc(nvbm::launch_rms(stream, hidden, residual, final_norm, normed, rows, H, c.rms_norm_eps),
@@ -278,6 +316,27 @@ int create_impl(NvbeModel* m, const NvbeModelConfig* cfg, const NvbeModelOptions
               "pinned sample buffer"));
   m->cu_q_host.resize(size_t(S) + 1);
   m->kv_lens_host.resize(size_t(S));
+  if (o.tc_gemms) {
+    if (H % 64 || (qh * D) % 64 || I % 64 || (qh + 2 * kvh) * D % 8 || I % 8)
+      return mfail("the tcgen05 GEMMs need hidden, attention and intermediate sizes that are multiples of 64");
+    const int mmax = std::min(nvbm::gemm_decode_max_rows(), T);
+    for (const auto& g : {std::array<int, 3>{(qh + 2 * kvh) * D, H, 0}, std::array<int, 3>{H, qh * D, 0},
+                          std::array<int, 3>{2 * I, H, 1}, std::array<int, 3>{H, I, 0}})
+      m->gemm_ws_bytes = std::max(m->gemm_ws_bytes, nvbm::gemm_decode_workspace(mmax, g[0], g[1], g[2] != 0, m->sms));
+    TRY(m->alloc(&m->gemm_ws, m->gemm_ws_bytes, "decode GEMM workspace"));
+    m->map_qkv.resize(size_t(L));
+    m->map_o.resize(size_t(L));
+    m->map_gate_up.resize(size_t(L));
+    m->map_down.resize(size_t(L));
+    for (int l = 0; l < L; ++l) {
+      const size_t i = size_t(l);
+      if (nvbm::gemm_weight_map(m->qkv_w[i], (qh + 2 * kvh) * D, H, false, &m->map_qkv[i]) ||
+          nvbm::gemm_weight_map(m->o_proj[i], H, qh * D, false, &m->map_o[i]) ||
+          nvbm::gemm_weight_map(m->gate_up_w[i], 2 * I, H, true, &m->map_gate_up[i]) ||
+          nvbm::gemm_weight_map(m->down_w[i], H, I, false, &m->map_down[i]))
+        return mfail("tensor maps of layer %d's weights (16-byte aligned BF16 [out, in] expected)", l);
+    }
+  }
   TRY(nvb_rc(nvb_rope_cache(m->stream, m->rope, o.max_model_len, D, c.rope_theta), "nvb_rope_cache"));
   return cuda_rc(cudaStreamSynchronize(m->stream), "model load synchronize");
 }
@@ -467,6 +526,30 @@ int nvbe_layer_gather(void* stream, const void* x, const int* indices, void* out
                                      sm_count()),
                  "gather launch");
 }
+
+size_t nvbe_gemm_workspace_bytes(int M, int N, int K, int silu) {
+  if (M < 1 || M > nvbm::gemm_decode_max_rows() || N < 4 || K < 64) return 0;
+  return nvbm::gemm_decode_workspace(M, N, K, silu != 0, sm_count());
+}
+
+int nvbe_layer_gemm(void* stream, const void* x, const void* w, void* y, int M, int N, int K, int silu,
+                    void* workspace, size_t workspace_bytes) {
+  g_model_error[0] = 0;
+  if (!x || !w || !y || M < 1 || M > nvbm::gemm_decode_max_rows() || N < 4 || N % (silu ? 8 : 4) || K < 64 ||
+      K % 64 || !aligned16(x) || !aligned16(w) || !aligned16(y))
+    return mfail("invalid decode GEMM arguments (M in [1, 256], K a multiple of 64, N of 4 or 8 with silu)");
+  const size_t need = nvbm::gemm_decode_workspace(M, N, K, silu != 0, sm_count());
+  if (!workspace || !aligned16(workspace) || workspace_bytes < need)
+    return mfail("the decode GEMM needs a 16-byte aligned workspace of %zu bytes (got %zu)", need, workspace_bytes);
+  CUtensorMap wmap, xmap;
+  if (nvbm::gemm_weight_map(w, N, K, silu != 0, &wmap) || nvbm::gemm_input_map(x, M, K, &xmap))
+    return mfail("decode GEMM tensor maps");
+  return cuda_rc(nvbm::launch_gemm_decode(static_cast<cudaStream_t>(stream), wmap, xmap, y, M, N, K,
+                                          silu ? N / 2 : N, silu != 0, sm_count(), workspace, workspace_bytes),
+                 "decode GEMM launch");
+}
+
+int nvbe_gemm_device_error(void) { return nvbm::gemm_decode_error(); }
 
 int nvbe_sample_partitions(int vocab) { return vocab > 0 ? nvbm::sample_partitions(vocab) : 0; }
 

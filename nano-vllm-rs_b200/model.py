@@ -29,7 +29,7 @@ class NvbeModelConfig(ctypes.Structure):
 
 class NvbeModelOptions(ctypes.Structure):
     _fields_ = [("device", I), ("block_size", I), ("num_blocks", I), ("max_batch_tokens", I),
-                ("max_sequences", I), ("max_model_len", I), ("cuda_graphs", I)]
+                ("max_sequences", I), ("max_model_len", I), ("cuda_graphs", I), ("tc_gemms", I)]
 
 
 class NvbeModelWeights(ctypes.Structure):
@@ -68,6 +68,10 @@ def library():
         L.nvbe_layer_add_rms.argtypes = [P] * 5 + [I, I, F]
         L.nvbe_layer_silu_mul.argtypes = [P] * 3 + [I, I]
         L.nvbe_layer_gather.argtypes = [P] * 4 + [I] * 3
+        L.nvbe_layer_gemm.argtypes = [P, P, P, P, I, I, I, I, P, ctypes.c_size_t]
+        L.nvbe_gemm_workspace_bytes.argtypes = [I, I, I, I]
+        L.nvbe_gemm_workspace_bytes.restype = ctypes.c_size_t
+        L.nvbe_gemm_device_error.argtypes = []
         L.nvbe_sample_partitions.argtypes = [I]
         L.nvbe_layer_sample.argtypes = [P] * 7 + [I, I]
         _lib = L
@@ -114,10 +118,11 @@ class ModelOptions:
     max_sequences: int = 32
     max_model_len: int = 4096
     cuda_graphs: bool = True
+    tc_gemms: bool = True  # tcgen05 GEMMs for forwards of <= 256 rows (else cuBLAS)
 
     def to_c(self):
         return NvbeModelOptions(self.device, self.block_size, self.num_blocks, self.max_batch_tokens,
-                                self.max_sequences, self.max_model_len, int(self.cuda_graphs))
+                                self.max_sequences, self.max_model_len, int(self.cuda_graphs), int(self.tc_gemms))
 
 
 def random_weights(config: Qwen3Config, seed=0, device="cuda", std=0.02):
@@ -272,6 +277,32 @@ def layer_silu_mul(packed, out, stream=None):
 def layer_gather(x, indices, out, stream=None):
     rows, hidden = out.shape
     _check(library().nvbe_layer_gather(_s(stream), _p(x), _p(indices), _p(out), rows, hidden, x.shape[0]))
+
+
+def gemm_workspace_bytes(m, n, k, silu=False):
+    return library().nvbe_gemm_workspace_bytes(m, n, k, int(silu))
+
+
+def layer_gemm(x, w, y, silu=False, stream=None, workspace=None):
+    """nvbe_layer_gemm: y = x w^T ([M, K] x [N, K] -> [M, N]) on the tcgen05
+    decode GEMM, or y[M, N / 2] = silu(gate) * up with silu=True. `workspace`
+    (a CUDA uint8 tensor of gemm_workspace_bytes) is allocated per call when
+    not given."""
+    import torch
+
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K or x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or y.dtype != torch.bfloat16:
+        raise ValueError("x [M, K], w [N, K] and y must be BF16 with matching K")
+    if tuple(y.shape) != (M, N // 2 if silu else N) or not (x.is_contiguous() and w.is_contiguous() and y.is_contiguous()):
+        raise ValueError("y must be a contiguous [M, N] (or [M, N / 2] with silu) tensor")
+    nbytes = library().nvbe_gemm_workspace_bytes(M, N, K, int(silu))
+    ws = workspace if workspace is not None else torch.empty(max(16, nbytes), dtype=torch.uint8, device=x.device)
+    _check(library().nvbe_layer_gemm(_s(stream), _p(x), _p(w), _p(y), M, N, K, int(silu), _p(ws), ws.numel()))
+
+
+def gemm_device_error():
+    return library().nvbe_gemm_device_error()
 
 
 def layer_sample(logits, temperatures, seeds, out, stream=None):
