@@ -44,6 +44,12 @@ typedef struct NvbeSchedulerConfig {
   size_t max_batch_tokens;
   int prefix_caching;
   int64_t eos_token_id;
+  /* 0: prefill and decode run in separate forwards, as the reference does
+   * (src/runtime.rs:557-565). 1: one forward takes every running
+   * sequence's decode token first, then prefill chunks under the same
+   * max_batch_tokens budget, so admitting a request does not stall decoding
+   * (the attention kernels take mixed query lengths in one launch). */
+  int mixed_batches;
 } NvbeSchedulerConfig;
 
 /* Request (src/runtime.rs:51-71). The prompt is borrowed for the call. */
@@ -93,6 +99,11 @@ typedef struct NvbeRunStats {
   double mean_ttft_ms;
   double mean_latency_ms;
   double mean_inter_token_latency_ms;
+  /* Forwards that held both decode rows and prefill rows (mixed_batches);
+   * their rows count in decode_tokens / prefill_tokens by kind and their
+   * time in mixed_seconds only. */
+  size_t mixed_steps;
+  double mixed_seconds;
 } NvbeRunStats;
 
 /* One forward pass: fill sampled[batch->samples]. Nonzero = failure. */

@@ -208,12 +208,20 @@ int NvbeEngine::execute(std::vector<Sequence>& seqs, uint64_t seed, NvbeRunStats
     if (active.empty()) return efail("scheduler made no progress");
 
     // Prefill and decode run as separate forwards; prefill is chunked by the
-    // token budget (src/runtime.rs:557-565).
+    // token budget (src/runtime.rs:557-565). With mixed_batches, decode rows
+    // come first and prefill chunks fill the rest of the budget.
     bool is_decode = true;
     for (size_t i : active) is_decode = is_decode && seqs[i].is_decode();
     candidates.clear();
-    for (size_t i : active)
-      if (seqs[i].is_decode() == is_decode) candidates.push_back(i);
+    if (config.mixed_batches) {
+      for (size_t i : active)
+        if (seqs[i].is_decode()) candidates.push_back(i);
+      for (size_t i : active)
+        if (!seqs[i].is_decode()) candidates.push_back(i);
+    } else {
+      for (size_t i : active)
+        if (seqs[i].is_decode() == is_decode) candidates.push_back(i);
+    }
     segments.clear();
     size_t budget = config.max_batch_tokens;
     for (size_t index : candidates) {
@@ -305,7 +313,11 @@ int NvbeEngine::execute(std::vector<Sequence>& seqs, uint64_t seed, NvbeRunStats
     batch.temperatures = temperatures.data();
     batch.seeds = seeds.data();
     batch.samples = out.samples;
-    batch.is_decode = is_decode ? 1 : 0;
+    size_t decode_rows = 0;
+    for (const Segment& seg : segments)
+      if (seqs[seg.sequence].is_decode()) decode_rows += seg.end - seg.start;
+    const bool all_decode = decode_rows == out.rows;
+    batch.is_decode = all_decode ? 1 : 0;
 
     const auto forward_started = clock::now();
     std::fill(sampled.begin(), sampled.begin() + long(out.samples), std::numeric_limits<uint32_t>::max());
@@ -315,14 +327,19 @@ int NvbeEngine::execute(std::vector<Sequence>& seqs, uint64_t seed, NvbeRunStats
     for (size_t k = 0; k < out.samples; ++k)
       if (sampled[k] > uint32_t(kI32Max)) return efail("model returned a token ID that does not fit in i32");
 
-    if (is_decode) {
+    if (all_decode) {
       stats.decode_steps += 1;
       stats.decode_tokens += out.rows;
       stats.decode_seconds += forward_seconds;
-    } else {
+    } else if (decode_rows == 0) {
       stats.prefill_steps += 1;
       stats.prefill_tokens += out.rows;
       stats.prefill_seconds += forward_seconds;
+    } else {
+      stats.mixed_steps += 1;
+      stats.decode_tokens += decode_rows;
+      stats.prefill_tokens += out.rows - decode_rows;
+      stats.mixed_seconds += forward_seconds;
     }
     const double now_ms = std::chrono::duration<double, std::milli>(clock::now() - started).count();
     size_t sample_index = 0;

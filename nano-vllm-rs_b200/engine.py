@@ -24,7 +24,7 @@ P = ctypes.c_void_p
 class NvbeSchedulerConfig(ctypes.Structure):
     _fields_ = [("block_size", c_size), ("num_blocks", c_size), ("max_sequences", c_size),
                 ("max_model_len", c_size), ("max_batch_tokens", c_size), ("prefix_caching", ctypes.c_int),
-                ("eos_token_id", ctypes.c_int64)]
+                ("eos_token_id", ctypes.c_int64), ("mixed_batches", ctypes.c_int)]
 
 
 class NvbeRequest(ctypes.Structure):
@@ -44,7 +44,8 @@ STAT_FIELDS = [("elapsed_seconds", ctypes.c_double), ("input_tokens", c_size), (
                ("decode_tokens", c_size), ("prefill_steps", c_size), ("decode_steps", c_size),
                ("prefill_seconds", ctypes.c_double), ("decode_seconds", ctypes.c_double),
                ("preemptions", c_size), ("peak_kv_blocks", c_size), ("mean_ttft_ms", ctypes.c_double),
-               ("mean_latency_ms", ctypes.c_double), ("mean_inter_token_latency_ms", ctypes.c_double)]
+               ("mean_latency_ms", ctypes.c_double), ("mean_inter_token_latency_ms", ctypes.c_double),
+               ("mixed_steps", c_size), ("mixed_seconds", ctypes.c_double)]
 
 
 class NvbeRunStats(ctypes.Structure):
@@ -91,11 +92,15 @@ class SchedulerConfig:
     max_batch_tokens: int = 1024
     prefix_caching: bool = True
     eos_token_id: int | None = None
+    # This build's addition: decode rows and prefill chunks in one forward
+    # (False keeps the reference's separate forwards).
+    mixed_batches: bool = False
 
     def to_c(self):
         return NvbeSchedulerConfig(self.block_size, self.num_blocks, self.max_sequences, self.max_model_len,
                                    self.max_batch_tokens, int(self.prefix_caching),
-                                   -1 if self.eos_token_id is None else int(self.eos_token_id))
+                                   -1 if self.eos_token_id is None else int(self.eos_token_id),
+                                   int(self.mixed_batches))
 
     def validate(self):
         c = self.to_c()

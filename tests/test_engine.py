@@ -213,6 +213,44 @@ def test_seed_is_independent_of_chunking_queueing_cache_and_preemption(max_seque
             assert o.token_ids == expected(req, 99)
 
 
+@pytest.mark.parametrize("mixed", [False, True])
+def test_mixed_batches_keep_outputs_and_budget(mixed):
+    # Eight requests through four sequence slots: sequences are admitted
+    # while others decode. Mixed forwards must give the same tokens (the
+    # runner's hash reads every context back through the page tables),
+    # respect the token budget, and decode in the forwards that prefill.
+    cfg = config(max_sequences=4, max_batch_tokens=6, num_blocks=48, mixed_batches=mixed)
+    engine, runner = engine_for(cfg)
+    reqs = [request(i, list(range(i, i + 2 + i % 5)), 3 + i % 4, temperature=0.5) for i in range(1, 9)]
+    out = engine.generate(reqs, 77)
+    for req, o in zip(reqs, out.outputs):
+        assert o.token_ids == expected(req, 77)
+    assert all(len(b.token_ids) <= cfg.max_batch_tokens for b in runner.batches)
+    st = out.stats
+    assert st["prefill_tokens"] + st["decode_tokens"] == sum(len(b.token_ids) for b in runner.batches)
+    assert st["prefill_steps"] + st["decode_steps"] + st["mixed_steps"] == len(runner.batches)
+    if mixed:
+        assert st["mixed_steps"] > 0 and st["mixed_seconds"] > 0
+    else:
+        assert st["mixed_steps"] == 0
+    assert engine.blocks_in_use() == 0
+
+
+def test_mixed_batches_take_fewer_forwards_and_survive_preemption():
+    reqs = [request(i, [i, i + 1, i + 2], 6) for i in range(1, 7)]
+    forwards = {}
+    for mixed in (False, True):
+        cfg = config(num_blocks=6, max_sequences=3, max_batch_tokens=4, max_model_len=10, prefix_caching=False,
+                     mixed_batches=mixed)
+        engine, runner = engine_for(cfg)
+        out = engine.generate(reqs, 3)
+        for req, o in zip(reqs, out.outputs):
+            assert o.token_ids == expected(req, 3)
+        assert engine.blocks_in_use() == 0
+        forwards[mixed] = len(runner.batches)
+    assert forwards[True] < forwards[False]
+
+
 def test_eos_stops_generation_and_ignore_eos_preserves_length():
     cfg = config(eos_token_id=42)
     engine, _ = engine_for(cfg, eos=42)
