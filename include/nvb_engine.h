@@ -159,8 +159,9 @@ typedef struct NvbeModelOptions {
   /* 1: projections of small forwards (decode steps of up to 16 sequences,
    * and up to 64 for projections of at most 2048 outputs, where it was
    * measured faster) run on this library's tcgen05 GEMM (nvbe_layer_gemm,
-   * SiLU fused into the gate/up projection); larger ones and the LM head use
-   * cuBLAS. 0: cuBLAS throughout. */
+   * SiLU fused into the gate/up projection), and steps sampling at most 4
+   * rows run the LM head with the sampler fused (nvbe_layer_gemm_sample);
+   * larger ones use cuBLAS. 0: cuBLAS throughout. */
   int tc_gemms;
 } NvbeModelOptions;
 
@@ -246,6 +247,19 @@ int nvbe_layer_gemm(void* stream, const void* x, const void* w, void* y, int M, 
 /* The decode GEMM's device error word: 0, or 1 when a pipeline wait gave up
  * (about two seconds); -1 if it cannot be read. */
 int nvbe_gemm_device_error(void);
+
+/* The LM head with Gumbel-max sampling fused into its epilogue (the
+ * reference runs cublasGemmEx, kernels/kernels.cu:98-106, then its sampler,
+ * kernels/kernels.cu:378-466): logits[M, N] = x[M, K] w[N, K]^T (BF16, as
+ * nvbe_layer_gemm rounds them) and out[M] = the sampled tokens, picked with
+ * the reference's SplitMix64 Gumbel stream exactly as nvbe_layer_sample
+ * picks them from those logits. The partial buffers hold
+ * M * nvbe_gemm_sample_tiles(N) entries each. M <= 256, K a multiple of
+ * 64, N of 4. */
+int nvbe_gemm_sample_tiles(int vocab);
+int nvbe_layer_gemm_sample(void* stream, const void* x, const void* w, void* logits, int M, int N, int K,
+                           const float* temperatures, const uint64_t* seeds, int* out, float* partial_scores,
+                           int* partial_indices);
 
 /* nv_sample_parallel: Gumbel-max sampling with the reference's SplitMix64
  * stream (temperature 0: argmax), ties to the lowest token id. The partial

@@ -36,6 +36,7 @@
 #include <mutex>
 
 #include "model_internal.cuh"
+#include "sample_math.cuh"
 
 namespace nvbm {
 
@@ -61,7 +62,13 @@ struct Params {
   int cluster;        // CTAs splitting one tile's K
   int stages;
   int silu;           // 0: Y[M, N]; 1: Y[M, N / 2] = silu(gate) * up
+  int sample;         // 1: Y = BF16 logits, plus each row's best Gumbel-max (score, token) per tile
   float* ws;          // FP32 partials [tiles][cluster][M][128] (L2-resident scratch)
+  const float* temps;       // sample: [M] temperatures
+  const uint64_t* seeds;    // sample: [M] seeds
+  float* part_score;        // sample: [M][tiles]
+  int* part_index;          // sample: [M][tiles]
+  int tiles;
   __nv_bfloat16* y;
   int ldy;            // elements per output row
 };
@@ -170,8 +177,14 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 
 enum { kBarFull = 0, kBarEmpty = kMaxStages, kBarDone = 2 * kMaxStages, kNumBars };
 constexpr int kTmemSlot = kNumBars * 8;
+constexpr int kSampleOff = 512;  // sampling epilogue: float [16][4] scores, int [16][4] tokens
+static_assert(kTmemSlot + 4 <= kSampleOff && kSampleOff + 16 * 4 * 8 <= kHeadBytes, "head layout overlaps");
 
-__global__ void __launch_bounds__(kThreads, 1)
+// kMode: 0 plain, 1 SiLU * up, 2 sampling (one instantiation each, so the
+// sampling epilogue carries no split-K registers and two of its CTAs share an
+// SM, overlapping one CTA's epilogue with the other's weight stream).
+template <int kMode>
+__global__ void __launch_bounds__(kThreads, kMode == 2 ? 2 : 1)
     gemm_decode_kernel(const Params p, const __grid_constant__ CUtensorMap wmap,
                        const __grid_constant__ CUtensorMap xmap) {
   // Launched as a programmatic dependent of the kernel before it: the next
@@ -215,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem_raw + kTmemSlot);
 
   // This CTA's FP32 partial [M][128] in the workspace: slot (tile, rank).
-  float* part = p.ws + ((long long)tile * p.cluster + rank) * p.M * kTileN;
+  float* part = kMode == 2 ? nullptr : p.ws + ((long long)tile * p.cluster + rank) * p.M * kTileN;
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && nkb > 0) {
@@ -227,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t dst = ring + s * stage_bytes;
         const int k = (kb0 + i) * kBK;
         mbar_expect_tx(full, uint32_t(stage_bytes));  // W and X bytes of the stage
-        if (p.silu) {
+        if (kMode == 1) {
           const int inter = p.N / 2, f0 = tile * (kTileN / 2);
           tma_load_2d(dst, &wmap, full, k, f0);                        // gate rows -> tile rows 0..63
           tma_load_2d(dst + kWBytes / 2, &wmap, full, k, inter + f0);  // up rows -> tile rows 64..127
@@ -280,7 +293,65 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool done = __all_sync(0xffffffffu, mbar_wait(bars + 8 * kBarDone, 0));
     tc_fence_after();
     const uint32_t taddr = tmem + (uint32_t(quad * 32) << 16);
-    for (int c = 0; c < p.M && done; c += 16) {
+    if constexpr (kMode == 2) {
+      // Logits of 128 tokens for every row: rounded to BF16 as the plain
+      // GEMM rounds them (stored, for the caller's diagnostics), scored with
+      // the sampler's Gumbel arithmetic, and folded to this tile's best
+      // (score, token) per row: warps, then the four warps through shared
+      // memory (named barrier 1 over the 128 epilogue threads).
+      using namespace sample_math;
+      float* slot_score = reinterpret_cast<float*>(smem_raw + kSampleOff);  // [16 rows][4 warps]
+      int* slot_index = reinterpret_cast<int*>(smem_raw + kSampleOff + 16 * 4 * 4);
+      const int n = tile * kTileN + f;
+      const int t = (warp - 2) * 32 + lane;
+      for (int c = 0; c < p.M; c += 16) {
+        uint32_t r[16];
+        if (done && nkb > 0) {
+          tmem_ld16(taddr + uint32_t(c), r);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) r[j] = 0u;
+        }
+        // The chunk's 16 scores first (independent: their latencies
+        // overlap), then the 16 warp folds.
+        float score[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = c + j;
+          score[j] = -INFINITY;
+          if (m < p.M && n < p.N) {
+            const __nv_bfloat16 lb = __float2bfloat16_rn(__uint_as_float(r[j]));
+            p.y[(long long)m * p.ldy + n] = lb;
+            score[j] = gumbel_score(__bfloat162float(lb), p.temps[m], p.seeds[m], n);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (c + j >= p.M) break;
+          float sc = score[j];
+          int index = n < p.N ? n : kNone;
+          warp_best(sc, index);
+          if (lane == 0) {
+            slot_score[j * 4 + quad] = sc;
+            slot_index[j * 4 + quad] = index;
+          }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (t < 16 && c + t < p.M) {
+          float best = slot_score[t * 4];
+          int best_index = slot_index[t * 4];
+          for (int q = 1; q < 4; ++q)
+            if (better(slot_score[t * 4 + q], slot_index[t * 4 + q], best, best_index)) {
+              best = slot_score[t * 4 + q];
+              best_index = slot_index[t * 4 + q];
+            }
+          p.part_score[(long long)(c + t) * p.tiles + tile] = best;
+          p.part_index[(long long)(c + t) * p.tiles + tile] = best_index;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+    }
+    for (int c = 0; c < p.M && done && kMode != 2; c += 16) {
       uint32_t r[16];
       if (nkb > 0) {
         tmem_ld16(taddr + uint32_t(c), r);
@@ -306,7 +377,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int m0 = rank * rows_per, rows = max(0, min(p.M, m0 + rows_per) - m0);
   const float* base = p.ws + (long long)tile * p.cluster * p.M * kTileN;
   const long long slot = (long long)p.M * kTileN;
-  if (!p.silu) {
+  if constexpr (kMode == 2) {
+    // done in the epilogue above
+  } else if constexpr (kMode == 0) {
     const int n0 = tile * kTileN;
     for (int e = threadIdx.x; e < rows * (kTileN / 4); e += kThreads) {
       const int m = m0 + e / (kTileN / 4), c4 = (e % (kTileN / 4)) * 4;
@@ -385,6 +458,11 @@ bool gemm_decode_preferred(int M, int N, int K) {
   return M >= 1 && (M <= 16 || (N <= 2048 && M <= 64));
 }
 
+// The LM head with the sampler fused (measured the same way against
+// cublasGemmEx + the sampler, vocabulary 151936): faster at one row (63.5
+// vs 68.5 us), even at 8, slower from 16 (the per-row scoring epilogue).
+bool gemm_sample_preferred(int M) { return M >= 1 && M <= 4; }
+
 namespace {
 
 // The kernel's shared-memory size and cluster-size attributes, once per
@@ -398,8 +476,10 @@ cudaError_t configure_kernel() {
   if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lock(mu);
   if (configured_device == dev) return cudaSuccess;
-  e = cudaFuncSetAttribute(gemm_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  for (auto fn : {gemm_decode_kernel<0>, gemm_decode_kernel<1>, gemm_decode_kernel<2>}) {
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  }
   if (e == cudaSuccess) configured_device = dev;
   return e;
 }
@@ -431,7 +511,7 @@ int max_clusters(int size) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    cache[size] = cudaOccupancyMaxActiveClusters(&n, gemm_detail::gemm_decode_kernel, &cfg) == cudaSuccess ? n : 0;
+    cache[size] = cudaOccupancyMaxActiveClusters(&n, gemm_detail::gemm_decode_kernel<0>, &cfg) == cudaSuccess ? n : 0;
   }
   return cache[size];
 }
@@ -464,6 +544,43 @@ size_t gemm_decode_workspace(int M, int N, int K, bool silu, int sms) {
   return tiles * size_t(gemm_decode_cluster(M, N, K, silu, sms)) * size_t(M) * kTileN * sizeof(float);
 }
 
+int gemm_decode_tiles(int N) { return (N + gemm_detail::kTileN - 1) / gemm_detail::kTileN; }
+
+namespace {
+cudaError_t launch_impl(cudaStream_t stream, const CUtensorMap& wmap, const CUtensorMap& xmap, gemm_detail::Params p,
+                        int tiles);
+}  // namespace
+
+cudaError_t launch_gemm_decode_sample(cudaStream_t stream, const CUtensorMap& wmap, const CUtensorMap& xmap,
+                                      void* logits, int M, int N, int K, const float* temps, const uint64_t* seeds,
+                                      float* part_score, int* part_index) {
+  using namespace gemm_detail;
+  if (M < 1 || M > 256 || N < 4 || N % 4 || K < kBK || K % kBK || !logits || !temps || !seeds || !part_score ||
+      !part_index || (reinterpret_cast<uintptr_t>(logits) & 7))
+    return cudaErrorInvalidValue;
+  if (cudaError_t e = configure_kernel(); e != cudaSuccess) return e;
+  Params p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.mpad = (M + 15) / 16 * 16;
+  p.kb_total = K / kBK;
+  p.sample = 1;
+  p.y = static_cast<__nv_bfloat16*>(logits);
+  p.ldy = N;
+  // Four stages: at most 16 rows that is 72 KB, so two CTAs share an SM
+  // (three, with three stages, measured no faster).
+  p.stages = kDataBytes / (kWBytes + p.mpad * 128);
+  if (p.stages > 4) p.stages = 4;
+  p.cluster = 1;  // each CTA holds whole logits for its tokens
+  p.temps = temps;
+  p.seeds = seeds;
+  p.part_score = part_score;
+  p.part_index = part_index;
+  p.tiles = gemm_decode_tiles(N);
+  return launch_impl(stream, wmap, xmap, p, p.tiles);
+}
+
 cudaError_t launch_gemm_decode(cudaStream_t stream, const CUtensorMap& wmap, const CUtensorMap& xmap, void* y,
                                int M, int N, int K, int ldy, bool silu, int sms, void* ws, size_t ws_bytes) {
   using namespace gemm_detail;
@@ -494,6 +611,14 @@ cudaError_t launch_gemm_decode(cudaStream_t stream, const CUtensorMap& wmap, con
   p.cluster = cluster;
   if (!ws || ws_bytes < gemm_decode_workspace(M, N, K, silu, sms)) return cudaErrorInvalidValue;
   p.ws = static_cast<float*>(ws);
+  return launch_impl(stream, wmap, xmap, p, tiles);
+}
+
+namespace {
+cudaError_t launch_impl(cudaStream_t stream, const CUtensorMap& wmap, const CUtensorMap& xmap, gemm_detail::Params p,
+                        int tiles) {
+  using namespace gemm_detail;
+  const int cluster = p.cluster;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = unsigned(cluster);
@@ -504,12 +629,17 @@ cudaError_t launch_gemm_decode(cudaStream_t stream, const CUtensorMap& wmap, con
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(unsigned(tiles * cluster));
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  // The ring holds p.stages stages; the split-K forms also reuse it for
+  // their receive space, so they take the whole budget.
+  cfg.dynamicSmemBytes = p.sample ? kHeadBytes + 1024 + p.stages * (kWBytes + p.mpad * 128) : kSmemBytes;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, gemm_decode_kernel, p, wmap, xmap);
+  if (p.sample) return cudaLaunchKernelEx(&cfg, gemm_decode_kernel<2>, p, wmap, xmap);
+  if (p.silu) return cudaLaunchKernelEx(&cfg, gemm_decode_kernel<1>, p, wmap, xmap);
+  return cudaLaunchKernelEx(&cfg, gemm_decode_kernel<0>, p, wmap, xmap);
 }
+}  // namespace
 
 int encode_map_2d(const void* base, uint64_t inner, uint64_t rows, uint32_t box_inner, uint32_t box_rows,
                   CUtensorMap* out) {

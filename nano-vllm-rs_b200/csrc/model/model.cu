@@ -102,7 +102,10 @@ struct NvbeModel {
   size_t last_samples = 0;
   // tcgen05 decode GEMMs: weight maps per layer, input maps per row count.
   std::vector<CUtensorMap> map_qkv, map_o, map_gate_up, map_down;
-  std::unordered_map<int, CUtensorMap> map_in[3];  // normed, attention, activated; keyed by rows
+  std::unordered_map<int, CUtensorMap> map_in[4];  // normed, attention, activated, gathered; keyed by rows
+  CUtensorMap map_lm{};  // LM head weights for the fused LM head + sampler
+  float* fused_score = nullptr;  // [max_sequences][tiles] per-tile bests of the fused sampler
+  int* fused_index = nullptr;
   void* gemm_ws = nullptr;  // split-K partials of the decode GEMMs
   size_t gemm_ws_bytes = 0;
 
@@ -131,7 +134,7 @@ int NvbeModel::gemm(const void* x, const void* w, void* y, int m, int n, int k) 
 int NvbeModel::tc_gemm(int which, const CUtensorMap& wmap, void* y, int m, int n, int k, bool silu) {
   auto it = map_in[which].find(m);
   if (it == map_in[which].end()) {
-    const void* x = which == 0 ? normed : which == 1 ? attention : activated;
+    const void* x = which == 0 ? normed : which == 1 ? attention : which == 2 ? activated : gathered;
     CUtensorMap map;
     if (nvbm::gemm_input_map(x, m, k, &map)) return mfail("decode GEMM input map (rows %d, K %d)", m, k);
     it = map_in[which].emplace(m, map).first;
@@ -206,10 +209,26 @@ int NvbeModel::forward(int rows, int sequences, int nsamples, int max_q, int max
     TRY(cuda_rc(nvbm::launch_rms(stream, hidden, residual, final_norm, normed, rows, H, c.rms_norm_eps),
                 "final add_rms_norm"));
     TRY(cuda_rc(nvbm::launch_gather(stream, normed, last_idx, gathered, nsamples, H, rows, sms), "gather"));
-    TRY(gemm(gathered, lm_head ? lm_head : embedding, logits, nsamples, c.vocab_size, H));
-    TRY(cuda_rc(nvbm::launch_sample(stream, logits, temps, seeds, samples, part_score, part_index, nsamples,
-                                    c.vocab_size),
-                "sample"));
+    if (o.tc_gemms && nvbm::gemm_sample_preferred(nsamples)) {
+      // LM head with the Gumbel-max sampler fused into its epilogue
+      auto it = map_in[3].find(nsamples);
+      if (it == map_in[3].end()) {
+        CUtensorMap map;
+        if (nvbm::gemm_input_map(gathered, nsamples, H, &map)) return mfail("LM head input map");
+        it = map_in[3].emplace(nsamples, map).first;
+      }
+      TRY(cuda_rc(nvbm::launch_gemm_decode_sample(stream, map_lm, it->second, logits, nsamples, c.vocab_size, H,
+                                                  temps, seeds, fused_score, fused_index),
+                  "fused LM head + sampler"));
+      TRY(cuda_rc(nvbm::launch_sample_combine(stream, fused_score, fused_index, samples, nsamples,
+                                              nvbm::gemm_decode_tiles(c.vocab_size)),
+                  "sample combine"));
+    } else {
+      TRY(gemm(gathered, lm_head ? lm_head : embedding, logits, nsamples, c.vocab_size, H));
+      TRY(cuda_rc(nvbm::launch_sample(stream, logits, temps, seeds, samples, part_score, part_index, nsamples,
+                                      c.vocab_size),
+                  "sample"));
+    }
   }
   return 0;
 }
@@ -324,6 +343,15 @@ int create_impl(NvbeModel* m, const NvbeModelConfig* cfg, const NvbeModelOptions
                           std::array<int, 3>{2 * I, H, 1}, std::array<int, 3>{H, I, 0}})
       m->gemm_ws_bytes = std::max(m->gemm_ws_bytes, nvbm::gemm_decode_workspace(mmax, g[0], g[1], g[2] != 0, m->sms));
     TRY(m->alloc(&m->gemm_ws, m->gemm_ws_bytes, "decode GEMM workspace"));
+    const size_t fused_parts = size_t(S) * size_t(nvbm::gemm_decode_tiles(c.vocab_size));
+    void* fp = nullptr;
+    TRY(m->alloc(&fp, fused_parts * 4, "fused sampler partials"));
+    m->fused_score = static_cast<float*>(fp);
+    TRY(m->alloc(&fp, fused_parts * 4, "fused sampler partials"));
+    m->fused_index = static_cast<int*>(fp);
+    if (c.vocab_size % 4 ||
+        nvbm::gemm_weight_map(m->lm_head ? m->lm_head : m->embedding, c.vocab_size, H, false, &m->map_lm))
+      return mfail("LM head tensor map (vocab a multiple of 4, 16-byte aligned weights)");
     m->map_qkv.resize(size_t(L));
     m->map_o.resize(size_t(L));
     m->map_gate_up.resize(size_t(L));
@@ -550,6 +578,28 @@ int nvbe_layer_gemm(void* stream, const void* x, const void* w, void* y, int M, 
 }
 
 int nvbe_gemm_device_error(void) { return nvbm::gemm_decode_error(); }
+
+int nvbe_gemm_sample_tiles(int vocab) { return vocab > 0 ? nvbm::gemm_decode_tiles(vocab) : 0; }
+
+int nvbe_layer_gemm_sample(void* stream, const void* x, const void* w, void* logits, int M, int N, int K,
+                           const float* temperatures, const uint64_t* seeds, int* out, float* partial_scores,
+                           int* partial_indices) {
+  g_model_error[0] = 0;
+  if (!x || !w || !logits || !temperatures || !seeds || !out || !partial_scores || !partial_indices || M < 1 ||
+      M > nvbm::gemm_decode_max_rows() || N < 4 || N % 4 || K < 64 || K % 64 || !aligned16(x) || !aligned16(w) ||
+      !aligned16(logits))
+    return mfail("invalid fused LM head arguments (M in [1, 256], K a multiple of 64, N of 4)");
+  CUtensorMap wmap, xmap;
+  if (nvbm::gemm_weight_map(w, N, K, false, &wmap) || nvbm::gemm_input_map(x, M, K, &xmap))
+    return mfail("fused LM head tensor maps");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = cuda_rc(nvbm::launch_gemm_decode_sample(s, wmap, xmap, logits, M, N, K, temperatures, seeds,
+                                                   partial_scores, partial_indices),
+                   "fused LM head launch");
+  if (rc) return rc;
+  return cuda_rc(nvbm::launch_sample_combine(s, partial_scores, partial_indices, out, M, nvbm::gemm_decode_tiles(N)),
+                 "sample combine launch");
+}
 
 int nvbe_sample_partitions(int vocab) { return vocab > 0 ? nvbm::sample_partitions(vocab) : 0; }
 

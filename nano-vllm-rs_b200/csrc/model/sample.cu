@@ -16,46 +16,17 @@
 #include <cstdint>
 
 #include "model_internal.cuh"
+#include "sample_math.cuh"
 
 namespace nvbm {
 
 namespace {
 
+using namespace sample_math;
+
 constexpr int kThreads = 256;
 constexpr int kPerThread = 16;
 constexpr int kPartition = kThreads * kPerThread;  // tokens per CTA
-constexpr int kNone = 0x7fffffff;
-
-__device__ __forceinline__ uint64_t splitmix64(uint64_t v) {
-  v += 0x9e3779b97f4a7c15ULL;
-  v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ULL;
-  v = (v ^ (v >> 27)) * 0x94d049bb133111ebULL;
-  return v ^ (v >> 31);
-}
-
-// (score, index) is better than (best, best_index).
-__device__ __forceinline__ bool better(float score, int index, float best, int best_index) {
-  return score > best || (score == best && index < best_index);
-}
-
-__device__ __forceinline__ void warp_best(float& score, int& index) {
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    const float s = __shfl_xor_sync(0xffffffffu, score, off);
-    const int i = __shfl_xor_sync(0xffffffffu, index, off);
-    if (better(s, i, score, index)) {
-      score = s;
-      index = i;
-    }
-  }
-}
-
-__device__ __forceinline__ float gumbel_score(float logit, float temperature, uint64_t seed, int token) {
-  if (!(temperature > 0.0f)) return logit;
-  const uint64_t x = splitmix64(seed ^ (uint64_t(token) * 0xd2b74407b1ce6e93ULL));
-  const float u = __fmul_rn(__fadd_rn(float(x >> 41), 0.5f), 1.0f / 8388608.0f);
-  return __fsub_rn(__fdiv_rn(logit, temperature), logf(-logf(u)));
-}
 
 // grid (partitions, rows): the best (score, index) of one partition of a row.
 __global__ void sample_partition_kernel(const __nv_bfloat16* __restrict__ logits, const float* __restrict__ temps,
@@ -131,6 +102,13 @@ cudaError_t launch_sample(cudaStream_t s, const void* logits, const float* temps
                                                                  seeds, part_score, part_index, vocab);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  sample_combine_kernel<<<(rows + 3) / 4, 128, 0, s>>>(part_score, part_index, out, rows, parts);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sample_combine(cudaStream_t s, const float* part_score, const int* part_index, int* out, int rows,
+                                  int parts) {
+  if (rows <= 0 || parts <= 0) return cudaErrorInvalidValue;
   sample_combine_kernel<<<(rows + 3) / 4, 128, 0, s>>>(part_score, part_index, out, rows, parts);
   return cudaGetLastError();
 }

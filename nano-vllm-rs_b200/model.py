@@ -72,6 +72,8 @@ def library():
         L.nvbe_gemm_workspace_bytes.argtypes = [I, I, I, I]
         L.nvbe_gemm_workspace_bytes.restype = ctypes.c_size_t
         L.nvbe_gemm_device_error.argtypes = []
+        L.nvbe_gemm_sample_tiles.argtypes = [I]
+        L.nvbe_layer_gemm_sample.argtypes = [P, P, P, P, I, I, I, P, P, P, P, P]
         L.nvbe_sample_partitions.argtypes = [I]
         L.nvbe_layer_sample.argtypes = [P] * 7 + [I, I]
         _lib = L
@@ -299,6 +301,23 @@ def layer_gemm(x, w, y, silu=False, stream=None, workspace=None):
     nbytes = library().nvbe_gemm_workspace_bytes(M, N, K, int(silu))
     ws = workspace if workspace is not None else torch.empty(max(16, nbytes), dtype=torch.uint8, device=x.device)
     _check(library().nvbe_layer_gemm(_s(stream), _p(x), _p(w), _p(y), M, N, K, int(silu), _p(ws), ws.numel()))
+
+
+def layer_gemm_sample(x, w, logits, temperatures, seeds, out, stream=None):
+    """nvbe_layer_gemm_sample: logits = x w^T and out = the Gumbel-max samples
+    of those logits (the reference sampler's stream), in one fused launch
+    plus the per-tile fold."""
+    import torch
+
+    M, K = x.shape
+    N = w.shape[0]
+    if tuple(logits.shape) != (M, N) or logits.dtype != torch.bfloat16 or out.shape[0] != M:
+        raise ValueError("logits must be [M, N] BF16 and out [M] int32")
+    tiles = library().nvbe_gemm_sample_tiles(N)
+    ps = torch.empty(M * tiles, dtype=torch.float32, device=x.device)
+    pi = torch.empty(M * tiles, dtype=torch.int32, device=x.device)
+    _check(library().nvbe_layer_gemm_sample(_s(stream), _p(x), _p(w), _p(logits), M, N, K, _p(temperatures),
+                                            _p(seeds), _p(out), _p(ps), _p(pi)))
 
 
 def gemm_device_error():

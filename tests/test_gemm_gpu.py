@@ -100,3 +100,29 @@ def test_gemm_rejects_invalid_shapes():
     y = torch.empty(257, 128, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(M_.ModelError):
         M_.layer_gemm(x, w, y)
+
+
+@pytest.mark.parametrize("m,n", [(8, 151936), (16, 20000), (1, 151936), (37, 20000)])
+def test_gemm_sample_fused_equals_unfused(m, n):
+    """The LM head with the Gumbel-max sampler fused into its epilogue gives
+    the same BF16 logits as the plain GEMM (both sum each logit in the same
+    order: more 128-token tiles than SMs, so neither splits K) and the same
+    tokens as the separate sampler on those logits, at temperature 0 and
+    above."""
+    k = 1024
+    x, w = _operands(m, n, k, seed=m * 3 + n)
+    x = (x.float() * 4).bfloat16()  # logits of a few units: near ties in the Gumbel scores
+    g = torch.Generator(device="cpu").manual_seed(m + n)
+    temps = torch.tensor([[0.0, 0.6, 1.0, 0.3][i % 4] for i in range(m)], dtype=torch.float32).cuda()
+    seeds = torch.randint(0, 2**62, (m,), generator=g, dtype=torch.int64).cuda()
+    plain = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    M_.layer_gemm(x, w, plain)
+    want = torch.empty(m, dtype=torch.int32, device="cuda")
+    M_.layer_sample(plain, temps, seeds, want)
+    logits = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    got = torch.empty(m, dtype=torch.int32, device="cuda")
+    M_.layer_gemm_sample(x, w, logits, temps, seeds, got)
+    torch.cuda.synchronize()
+    assert M_.gemm_device_error() == 0
+    assert (bits(logits) == bits(plain)).all()
+    assert got.tolist() == want.tolist()
