@@ -156,7 +156,7 @@ typedef struct NvbeModelOptions {
   int max_sequences;
   int max_model_len;
   int cuda_graphs;
-  /* 1: projections of small forwards (decode steps of up to 16 sequences,
+  /* 1: projections of small forwards (decode steps of up to 8 sequences,
    * and up to 64 for projections of at most 2048 outputs, where it was
    * measured faster) run on this library's tcgen05 GEMM (nvbe_layer_gemm,
    * SiLU fused into the gate/up projection), and steps sampling at most 4

@@ -197,6 +197,16 @@ int kv_mma_map(const void* cache, long long tokens, int kvh, CUtensorMap* out, u
   return make_map_3d(cache, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, out);
 }
 
+// tcgen05 decode queries: [rows][qh][128] with a {64, 16, 1} box, 128B
+// swizzle (one row's 16 heads from the head group's first; heads past qh are
+// zero fill).
+int q_mma_map(const void* q, int rows, int qh, CUtensorMap* out) {
+  const uint64_t dims[3] = {128, uint64_t(qh), uint64_t(rows)};
+  const uint64_t strides[2] = {256, uint64_t(qh) * 256};
+  const uint32_t box[3] = {64, 16, 1};
+  return make_map_3d(q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, out);
+}
+
 // `combine` false leaves split-KV partials in lse_accum / out_accum for the
 // caller's own combine (the multi-GPU gather path); only the tensor-core
 // decode can stop there.
@@ -211,7 +221,17 @@ int run_decode(cudaStream_t stream, DecodeParams p, const void* k, const void* v
     if (int rc = kv_mma_map(k, tokens, p.kvh, &khalf, 64)) return rc;
     if (int rc = kv_mma_map(v, tokens, p.kvh, &vhalf, 64)) return rc;
     p.n_hgroups = (p.qh / p.kvh + 15) / 16;
-    cudaError_t e = launch_decode_mma(p, kmap, vmap, khalf, vhalf, stream);
+    // Short contexts (an engine's decode batch: max_k bounded by its model
+    // length) take the persistent schedule; long ones one CTA per item,
+    // measured faster for them.
+    cudaError_t e;
+    if (p.max_k > 0 && p.max_k <= kPersistentMaxK) {
+      CUtensorMap qmap;
+      if (int rc = q_mma_map(p.q, p.rows, p.qh, &qmap)) return rc;
+      e = launch_decode_persistent(p, kmap, vmap, khalf, vhalf, qmap, stream);
+    } else {
+      e = launch_decode_mma(p, kmap, vmap, khalf, vhalf, stream);
+    }
     if (e != cudaErrorNotSupported) {
       if (e == cudaSuccess && p.num_splits > 1 && combine) e = launch_combine(p, stream);
       return cuda_status(e, "decode attention launch");
@@ -294,6 +314,7 @@ int paged_fwd_impl(void* stream, const void* q, const void* k, const void* v, vo
   p.num_splits = num_splits;
   p.max_q = 1;
   p.mode = kModeDecode;
+  p.max_k = max_k;
   return run_decode(s, p, k, v, combine);
 }
 

@@ -107,6 +107,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* desc, uint64_
       : "memory");
 }
 
+// 3-D tiled TMA load with the default L2 policy into a shared-memory
+// address (the persistent decode's per-item query tile).
+__device__ __forceinline__ void tma_load_3d_plain(uint32_t dst, const void* desc, uint64_t* bar, int c0, int c1,
+                                                  int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 // Same, with an L2 eviction-priority hint (createpolicy result).
 __device__ __forceinline__ void tma_load_3d_hint(void* dst, const void* desc, uint64_t* bar, int c0, int c1,
                                                  int c2, uint64_t policy) {

@@ -32,6 +32,7 @@ struct DecodeParams {
   int rows, qh, kvh, block_size, table_stride, num_blocks, batch, max_context;
   int num_splits, n_hgroups, max_q;
   int mode;
+  int max_k;         // decode: the caller's bound on kv_lens (picks the decode schedule)
   float scale_log2;  // log2(e) / sqrt(128)
 };
 
@@ -42,6 +43,13 @@ cudaError_t launch_decode(DecodeParams p, const CUtensorMap& kmap, const CUtenso
 // box and the same maps with a {64, 1, 64} box for short last tiles.
 cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                               const CUtensorMap& kmap_half, const CUtensorMap& vmap_half, cudaStream_t stream);
+// Persistent form of the tcgen05 decode (decode_persistent.cu), for short
+// contexts: same arguments plus the query map.
+cudaError_t launch_decode_persistent(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                                     const CUtensorMap& kmap_half, const CUtensorMap& vmap_half,
+                                     const CUtensorMap& qmap, cudaStream_t stream);
+// Decode batches whose max_k is at most this use the persistent form.
+constexpr int kPersistentMaxK = 2048;
 int decode_group_chunk(int group);
 // Split-KV combine of lse_accum / out_accum into out (and lse).
 cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream);

@@ -449,13 +449,14 @@ __global__ void __launch_bounds__(kThreads, kMode == 2 ? 2 : 1)
 int gemm_decode_max_rows() { return 256; }
 
 // Measured against cublasGemmEx in CUDA graphs on B200 (Qwen3-0.6B shapes,
-// weights streamed from HBM): this kernel is faster up to 16 rows for every
-// projection, and up to 64 rows for outputs of at most 2048 features (few
-// tiles, so K splits over large clusters); past that the split-K partials,
-// which grow with the rows, cost more than cuBLAS's whole GEMM.
+// weights streamed from HBM): this kernel is faster up to 8 rows for every
+// projection (the 4096-output QKV projection drew level at 16), and up to 64
+// rows for outputs of at most 2048 features (few tiles, so K splits over
+// large clusters); past that the split-K partials, which grow with the rows,
+// cost more than cuBLAS's whole GEMM.
 bool gemm_decode_preferred(int M, int N, int K) {
   (void)K;
-  return M >= 1 && (M <= 16 || (N <= 2048 && M <= 64));
+  return M >= 1 && (M <= 8 || (N <= 2048 && M <= 64));
 }
 
 // The LM head with the sampler fused (measured the same way against

@@ -24,7 +24,7 @@ SHAPES = [("qkv", 4096, 1024, False), ("o", 1024, 2048, False), ("gate_up_silu",
           ("down", 1024, 3072, False)]
 ROWS = [1, 8, 16, 32, 64, 128, 256]
 PREFERRED = {  # the model's dispatch rule (gemm_decode_preferred)
-    (name, m): (m <= 16 or (n <= 2048 and m <= 64)) for name, n, _, _ in SHAPES for m in ROWS}
+    (name, m): (m <= 8 or (n <= 2048 and m <= 64)) for name, n, _, _ in SHAPES for m in ROWS}
 
 
 def _graph_time(fn, copies, reps=4):
