@@ -501,6 +501,7 @@ def main():
 
     # ---------------- end to end through the public API, host buffers
     e2e_value = e2e_ms = None
+    e2e_breakdown = None
     e2e_sizes = None
     h2d = d2h = 0
     e2e_steps = 1
@@ -632,6 +633,45 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = t.item()
         e2e_value = world * step_bytes / (e2e_ms / e2e_steps / 1e3) / 1e9
+
+        # Untimed diagnostics (max over ranks, all ranks at once, as in the
+        # timed loop): the step's host-to-device copy alone, its kernels alone
+        # (inputs already on the device) and its device-to-host copy alone.
+        def alone(s, fn, n=20):
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_.record(s)
+            for _ in range(n):
+                fn()
+            b_.record(s)
+            torch.cuda.synchronize()
+            t_ = torch.tensor([a_.elapsed_time(b_) / n], device=dev)
+            if world > 1:
+                dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+            return t_.item()
+
+        def kernels_only():
+            for (s0, s1, sp, la_c, oa_c) in chunk_cfg:
+                n = s1 - s0
+                nvb.qkv_rope_cached(dev_in["qkv"][s0:s1], qw, kw, dev_in["pos"][s0:s1], dev_in["slots"][s0:s1],
+                                    q_dev[s0:s1], case.k, case.v, rows=n, q_heads=QH, kv_heads=KVH, head_dim=DIM,
+                                    block_size=BS, num_blocks=case.num_blocks, eps=1e-6, rope_cache=rope,
+                                    max_positions=CTX)
+                nvb.paged_fwd(q_dev[s0:s1], case.k, case.v, out[s0:s1], dev_in["cuq"][:n + 1], dev_in["lens"][s0:s1],
+                              dev_in["table"][s0:s1], batch=n, max_q=1, max_k=CTX, q_heads=QH, kv_heads=KVH,
+                              block_size=BS, table_stride=case.table_stride, num_blocks=case.num_blocks,
+                              num_splits=sp, lse=lse[s0:s1], lse_accum=la_c, out_accum=oa_c)
+
+        with torch.cuda.stream(h2d_s):
+            h2d_ms = alone(h2d_s, lambda: stage_d.copy_(stage_h, non_blocking=True))
+        with torch.cuda.stream(d2h_s):
+            d2h_ms = alone(d2h_s, lambda: out_h.copy_(out, non_blocking=True))
+        kern_ms = alone(stream, kernels_only)
+        e2e_breakdown = {"step_ms": round(e2e_ms / e2e_steps, 5), "h2d_ms": round(h2d_ms, 5),
+                         "h2d_gbs": round(total / (h2d_ms / 1e3) / 1e9, 2), "kernels_ms": round(kern_ms, 5),
+                         "d2h_ms": round(d2h_ms, 5), "d2h_gbs": round(d2h / (d2h_ms / 1e3) / 1e9, 2)}
         del qkv_h, dev_in
 
     # ---------------- prefill TFLOP/s (config 2: full prompts, then the
@@ -735,6 +775,7 @@ def main():
             "e2e": None if e2e_value is None else {
                 "value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms / e2e_steps, 5), "chunks": nch, "chunk_sizes": e2e_sizes,
+                "breakdown": e2e_breakdown,
                 "path": "per sequence chunk: pinned H2D of step inputs -> nvb_qkv_rope_cached -> nvb_paged_fwd_ex -> "
                         "D2H output, chunks pipelined on H2D / compute / D2H streams"},
             "gpu_launches": args.steps * (1 if splits == 1 else 2),
