@@ -11,6 +11,7 @@
 //   request validation   src/runtime.rs:411-455
 // The model is reached through NvbeRunFn, so the same scheduler drives the
 // GPU runner (libnvb_model.so) and the CPU test runners.
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdarg>
@@ -221,6 +222,15 @@ int NvbeEngine::execute(std::vector<Sequence>& seqs, uint64_t seed, NvbeRunStats
     } else {
       for (size_t i : active)
         if (seqs[i].is_decode() == is_decode) candidates.push_back(i);
+    }
+    if (is_decode) {
+      // Longest context first: the attention kernels claim (sequence, kv
+      // head) items in row order, so a step ends on short items instead of
+      // a long one started last. Rows are independent, so the order changes
+      // no result.
+      std::stable_sort(candidates.begin(), candidates.end(), [&](size_t a, size_t b) {
+        return seqs[a].tokens.size() > seqs[b].tokens.size();
+      });
     }
     segments.clear();
     size_t budget = config.max_batch_tokens;
