@@ -41,7 +41,8 @@ __device__ __forceinline__ void warp_best(float& score, int& index) {
 __device__ __forceinline__ float gumbel_score(float logit, float temperature, uint64_t seed, int token) {
   if (!(temperature > 0.0f)) return logit;
   const uint64_t x = splitmix64(seed ^ (uint64_t(token) * 0xd2b74407b1ce6e93ULL));
-  const float u = __fmul_rn(__fadd_rn(float(x >> 41), 0.5f), 1.0f / 8388608.0f);
+  // x >> 41 has 23 bits: its 32-bit conversion is exact, like the 64-bit one.
+  const float u = __fmul_rn(__fadd_rn(float(uint32_t(x >> 41)), 0.5f), 1.0f / 8388608.0f);
   return __fsub_rn(__fdiv_rn(logit, temperature), logf(-logf(u)));
 }
 
