@@ -100,6 +100,7 @@ constexpr int kItemReaders = 15;
 constexpr int kTmemSlotOff = kNumBars * 8;
 constexpr int kItemOff = 320;                               // Item [2] (the published-item ring)
 constexpr int kItemBytes = 64;
+constexpr int kVRealOff = 448;                              // int [2]: real keys of the V tile in each stage
 constexpr int kStatsOff = 512;                              // float2 [2][128]: row max used, row sum
 constexpr int kMaxSorted = 1024;                            // batches up to this size are claimed by work
 constexpr int kOrderOff = kStatsOff + 2 * kRows * 8;        // int [kMaxSorted]: sequences, heaviest first
@@ -110,7 +111,8 @@ constexpr int kKOff = kQOff + kQStages * kQBytes;
 constexpr int kVOff = kKOff + kKStages * kKVBytes;
 constexpr int kTileBytes = kVOff + kVStages * kKVBytes;     // 192 KB
 constexpr int kSmemBytes = kTileBytes + kHeadBytes + 1024;  // + worst-case alignment pad
-static_assert(kTmemSlotOff + 4 <= kItemOff && kItemOff + 2 * kItemBytes <= kStatsOff, "head layout overlaps");
+static_assert(kTmemSlotOff + 4 <= kItemOff && kItemOff + 2 * kItemBytes <= kVRealOff && kVRealOff + 8 <= kStatsOff,
+              "head layout overlaps");
 static_assert(kSmemBytes <= 232448, "tile layout exceeds the per-CTA shared memory limit");
 
 struct PrefillParams {
@@ -367,6 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(head + kTmemSlotOff);
   Item* ring = reinterpret_cast<Item*>(head + kItemOff);
   float2* stats = reinterpret_cast<float2*>(head + kStatsOff);
+  volatile int* v_real = reinterpret_cast<volatile int*>(head + kVRealOff);
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
@@ -554,6 +557,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             unsigned char* vdst = tiles + kVOff + st * kKVBytes;
+            // keys of the tile that are real (the fixer zeroes the rest); the
+            // arrival below releases the store to the fixer's wait
+            v_real[st] = ok ? min(kKeys, it.kv_len - key0) : 0;
             if (ok) {
               mbar_arrive_expect_tx(&bars[kVFull + st], kKVBytes);
               tma_load_3d(vdst, &vmap, &bars[kVFull + st], 0, it.h, trow);
@@ -630,16 +636,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       Item it;
       for (int i = 0; alive && take_item(bars, ring, i, true, it); ++i) {
         const int nt = item_tiles(it);
-        const int* table = p.block_table + (long long)it.b * p.table_stride;
         for (int j = 0; j < nt; ++j) {
           const int g = gt + j, st = g & 1;
-          const int key0 = j * kKeys;
-          const bool ok = page_ok(table[p.fd_bs.div(key0)], p.num_blocks);
-          const int real = ok ? min(kKeys, it.kv_len - key0) : 0;
           if (!warp_wait(&bars[kVFull + st], (g >> 1) & 1)) {
             alive = false;
             break;
           }
+          const int real = v_real[st];  // written by the V producer before its arrival
           if (real < kKeys) {
             const uint32_t vbase = sbase + kVOff + st * kKVBytes;
             for (int e = lane; e < (kKeys - real) * 16; e += 32) {
@@ -734,6 +737,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld16(lane_base + kOCol + x * kKeys + h * 16, o);
             tmem_ld_wait();
             reg_fence(o);
+            if (h == 7) {
+              // O_x is read: free it for the next item's first PV before the last stores.
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&bars[kOFree + x]);
+            }
             if (valid_row) {
 #pragma unroll
               for (int vv = 0; vv < 2; ++vv) {
@@ -747,9 +756,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars[kOFree + x]);
           if (valid_row && lse_dst) {
             const float m_out = ml.x == -INFINITY ? 0.0f : ml.x;
             *lse_dst = l > 0.0f ? (m_out + fast_log2(l)) * kLn2 : -INFINITY;
