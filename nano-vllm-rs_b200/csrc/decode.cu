@@ -34,6 +34,7 @@
 //    CTA writes the final BF16 output (1 split) or a normalised FP32 partial
 //    plus its natural-log LSE (several splits) for the combine kernel.
 #include "internal.cuh"
+#include "combine.cuh"
 
 namespace nvb {
 
@@ -405,39 +406,27 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const DecodeParams p,
   }
 }
 
-// One warp per (row, q head): weights each split's normalised partial by
-// exp(lse_s - max_s lse_s) (kernels/decode_candidate.cuh:180-201 restated in
-// LSE form) and writes BF16 output plus the final LSE.
-__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ lse_accum,
-                                                      const float* __restrict__ out_accum,
-                                                      __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
-                                                      int rows, int qh, int splits, int lse_stride) {
+// W warps per (row, q head) item (combine.cuh): each split's normalised
+// partial weighted by exp(lse_s - max_s lse_s) (kernels/decode_candidate.cuh:
+// 180-201 restated in LSE form); BF16 output plus the final LSE.
+template <int W>
+__global__ void __launch_bounds__(combine_detail::kCombineThreads)
+    combine_kernel(const float* __restrict__ lse_accum, const float* __restrict__ out_accum,
+                   __nv_bfloat16* __restrict__ out, float* __restrict__ lse, int rows, int qh, int splits,
+                   int lse_stride) {
   // Launched as a programmatic dependent of the decode grid: wait until that
   // grid has completed and its partials are visible (a no-op otherwise).
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (item >= (long long)rows * qh) return;
-  const long long stride = (long long)rows * qh;
-  float mx = -INFINITY;
-  for (int s = lane; s < splits; s += 32) mx = fmaxf(mx, lse_accum[s * stride + item]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = warp % W;
+  const long long item = (long long)blockIdx.x * (combine_detail::kCombineThreads / 32 / W) + warp / W;
+  const bool live = item < (long long)rows * qh;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float total = 0.0f;
-  if (mx != -INFINITY) {
-    for (int s = 0; s < splits; ++s) {
-      const float ls = lse_accum[s * stride + item];
-      if (ls == -INFINITY) continue;
-      const float w = __expf(ls - mx);
-      total += w;
-      const float4 v = *reinterpret_cast<const float4*>(out_accum + (s * stride + item) * 128 + lane * 4);
-      acc.x = fmaf(w, v.x, acc.x);
-      acc.y = fmaf(w, v.y, acc.y);
-      acc.z = fmaf(w, v.z, acc.z);
-      acc.w = fmaf(w, v.w, acc.w);
-    }
-  }
+  float total = 0.0f, mx = -INFINITY;
+  if (live)
+    combine_detail::combine_share<W>(lse_accum, out_accum, item, (long long)rows * qh, splits, sub, lane, acc, total,
+                                     mx);
+  combine_detail::combine_gather_shares<W>(acc, total, warp, lane, sub);
+  if (!live || sub != 0) return;
   const float inv = total > 0.0f ? 1.0f / total : 0.0f;
   uint2 packed;
   packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
@@ -496,12 +485,14 @@ cudaError_t launch_decode(DecodeParams p, const CUtensorMap& kmap, const CUtenso
 cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream) {
   using namespace decode_detail;
   const long long items = (long long)p.rows * p.qh;
-  const long long grid = (items + 7) / 8;
+  const int w = combine_detail::combine_warps(p.num_splits);
+  const int per_cta = combine_detail::kCombineThreads / 32 / w;  // items a CTA combines
+  const long long grid = (items + per_cta - 1) / per_cta;
   // Programmatic stream serialization: the combine's launch overlaps the
   // decode grid's tail instead of following its completion.
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(unsigned(grid));
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(combine_detail::kCombineThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -509,9 +500,15 @@ cudaError_t launch_combine(const DecodeParams& p, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, combine_kernel, static_cast<const float*>(p.lse_accum),
-                            static_cast<const float*>(p.out_accum), p.out, p.lse, p.rows, p.qh, p.num_splits,
-                            p.max_q);
+  const float* la = static_cast<const float*>(p.lse_accum);
+  const float* oa = static_cast<const float*>(p.out_accum);
+  switch (w) {
+    case 1: return cudaLaunchKernelEx(&cfg, combine_kernel<1>, la, oa, p.out, p.lse, p.rows, p.qh, p.num_splits, p.max_q);
+    case 2: return cudaLaunchKernelEx(&cfg, combine_kernel<2>, la, oa, p.out, p.lse, p.rows, p.qh, p.num_splits, p.max_q);
+    case 4: return cudaLaunchKernelEx(&cfg, combine_kernel<4>, la, oa, p.out, p.lse, p.rows, p.qh, p.num_splits, p.max_q);
+    default:
+      return cudaLaunchKernelEx(&cfg, combine_kernel<8>, la, oa, p.out, p.lse, p.rows, p.qh, p.num_splits, p.max_q);
+  }
 }
 
 }  // namespace nvb

@@ -16,6 +16,7 @@
 // no library kernel touches peer memory: only plain stores and the flags.
 // The barrier's waits are bounded (kWaitCycles) and record kErrGatherWait.
 #include "internal.cuh"
+#include "combine.cuh"
 
 namespace nvb {
 
@@ -56,61 +57,46 @@ __device__ __forceinline__ void exchange_epoch(const PeerPtrs& peers, int world,
   }
 }
 
-// One warp per (row, local head). splits > 1: weights split s by
-// exp(lse_s - max lse) like combine_kernel (decode.cu); splits == 1: copies
-// the local decode output. The result goes to every rank at head offset
-// head_offset (= rank * qh local).
+// W warps per (row, local head) item (combine.cuh). splits > 1: weights
+// split s by exp(lse_s - max lse) exactly as combine_kernel (decode.cu) does;
+// splits == 1: copies the local decode output. The result goes to every rank
+// at head offset head_offset (= rank * qh local).
 // kBarrier (the counter form): the CTA that finishes last (a done count in
 // the rank's flag slot world + 1; every CTA fences its peer stores at system
 // scope before counting) runs the epoch exchange itself, advances the device
 // epoch and resets the count, so the step needs no separate barrier launch.
-template <bool kBarrier>
-__global__ void __launch_bounds__(256) combine_gather_kernel(const float* __restrict__ lse_accum,
-                                                             const float* __restrict__ out_accum,
-                                                             const __nv_bfloat16* __restrict__ local_out, int rows,
-                                                             int qh, int splits, PeerPtrs peers, int world,
-                                                             int head_offset, int qh_total, unsigned int* counter,
-                                                             int rank) {
+template <bool kBarrier, int W>
+__global__ void __launch_bounds__(combine_detail::kCombineThreads)
+    combine_gather_kernel(const float* __restrict__ lse_accum, const float* __restrict__ out_accum,
+                          const __nv_bfloat16* __restrict__ local_out, int rows, int qh, int splits, PeerPtrs peers,
+                          int world, int head_offset, int qh_total, unsigned int* counter, int rank) {
   // Launched as a programmatic dependent of the decode grid (see
   // nvb_paged_decode_gather): the barrier kernel after it may be scheduled
   // now, and this grid waits for the decode to complete before reading.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (item < (long long)rows * qh) {
-  uint2 packed;
-  if (splits > 1) {
-    const long long stride = (long long)rows * qh;
-    float mx = -INFINITY;
-    for (int s = lane; s < splits; s += 32) mx = fmaxf(mx, lse_accum[s * stride + item]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float total = 0.0f;
-    if (mx != -INFINITY) {
-      for (int s = 0; s < splits; ++s) {
-        const float ls = lse_accum[s * stride + item];
-        if (ls == -INFINITY) continue;
-        const float w = __expf(ls - mx);
-        total += w;
-        const float4 v = *reinterpret_cast<const float4*>(out_accum + (s * stride + item) * 128 + lane * 4);
-        acc.x = fmaf(w, v.x, acc.x);
-        acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z);
-        acc.w = fmaf(w, v.w, acc.w);
-      }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = warp % W;
+  const long long item = (long long)blockIdx.x * (combine_detail::kCombineThreads / 32 / W) + warp / W;
+  const bool live = item < (long long)rows * qh;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float total = 0.0f, mx = -INFINITY;
+  if (live && splits > 1)
+    combine_detail::combine_share<W>(lse_accum, out_accum, item, (long long)rows * qh, splits, sub, lane, acc, total,
+                                     mx);
+  combine_detail::combine_gather_shares<W>(acc, total, warp, lane, sub);
+  if (live && sub == 0) {
+    uint2 packed;
+    if (splits > 1) {
+      const float inv = total > 0.0f ? 1.0f / total : 0.0f;
+      packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+      packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+    } else {
+      packed = *reinterpret_cast<const uint2*>(local_out + item * 128 + lane * 4);
     }
-    const float inv = total > 0.0f ? 1.0f / total : 0.0f;
-    packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-    packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-  } else {
-    packed = *reinterpret_cast<const uint2*>(local_out + item * 128 + lane * 4);
-  }
-  const long long row = item / qh, h = item - row * qh;
-  const long long dst = (row * qh_total + head_offset + h) * 128 + lane * 4;
-  const int set = counter ? int(step_epoch(0, counter) & 1u) : 0;
-  for (int p = 0; p < world; ++p) *reinterpret_cast<uint2*>(peers.out[set][p] + dst) = packed;
+    const long long row = item / qh, h = item - row * qh;
+    const long long dst = (row * qh_total + head_offset + h) * 128 + lane * 4;
+    const int set = counter ? int(step_epoch(0, counter) & 1u) : 0;
+    for (int p = 0; p < world; ++p) *reinterpret_cast<uint2*>(peers.out[set][p] + dst) = packed;
   }
   __threadfence_system();  // the stores are visible to the peers before this thread ends
   if constexpr (kBarrier) {
@@ -196,6 +182,27 @@ extern "C" int nvb_peer_buffer_free(void* ptr) {
 namespace nvb {
 namespace gather_detail {
 
+// combine_gather_kernel with W warps per item (combine_detail::combine_warps).
+template <bool kBarrier>
+cudaError_t launch_combine_gather(const cudaLaunchConfig_t& cfg, int w, const float* la, const float* oa,
+                                  const __nv_bfloat16* lo, int rows, int qh, int splits, PeerPtrs peers, int world,
+                                  int head_offset, int qh_total, unsigned int* counter, int rank) {
+  switch (w) {
+    case 1:
+      return cudaLaunchKernelEx(&cfg, combine_gather_kernel<kBarrier, 1>, la, oa, lo, rows, qh, splits, peers, world,
+                                head_offset, qh_total, counter, rank);
+    case 2:
+      return cudaLaunchKernelEx(&cfg, combine_gather_kernel<kBarrier, 2>, la, oa, lo, rows, qh, splits, peers, world,
+                                head_offset, qh_total, counter, rank);
+    case 4:
+      return cudaLaunchKernelEx(&cfg, combine_gather_kernel<kBarrier, 4>, la, oa, lo, rows, qh, splits, peers, world,
+                                head_offset, qh_total, counter, rank);
+    default:
+      return cudaLaunchKernelEx(&cfg, combine_gather_kernel<kBarrier, 8>, la, oa, lo, rows, qh, splits, peers, world,
+                                head_offset, qh_total, counter, rank);
+  }
+}
+
 int gather_impl(void* stream, const void* q, const void* k, const void* v, void* out_local, const int* cu_q,
                 const int* kv_lens, const int* block_table, int batch, int max_k, int q_heads, int kv_heads,
                 int block_size, int table_stride, int num_blocks, int num_splits, float* lse_accum, float* out_accum,
@@ -232,26 +239,26 @@ int gather_impl(void* stream, const void* q, const void* k, const void* v, void*
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  const int splits = partials ? num_splits : 1;
+  const int w = combine_detail::combine_warps(splits);
+  const int per_cta = combine_detail::kCombineThreads / 32 / w;  // items a CTA combines
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(unsigned((items + 7) / 8));
-  cfg.blockDim = dim3(256);
+  cfg.gridDim = dim3(unsigned((items + per_cta - 1) / per_cta));
+  cfg.blockDim = dim3(combine_detail::kCombineThreads);
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  const float* la = static_cast<const float*>(lse_accum);
+  const float* oa = static_cast<const float*>(out_accum);
+  const __nv_bfloat16* lo = static_cast<const __nv_bfloat16*>(out_local);
   if (counter) {
     // Counter form: the combine's last CTA runs the epoch exchange.
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, combine_gather_kernel<true>, static_cast<const float*>(lse_accum),
-                                             static_cast<const float*>(out_accum),
-                                             static_cast<const __nv_bfloat16*>(out_local), batch, q_heads,
-                                             partials ? num_splits : 1, peers, world, rank * q_heads,
-                                             world * q_heads, counter, rank);
+    const cudaError_t e = launch_combine_gather<true>(cfg, w, la, oa, lo, batch, q_heads, splits, peers, world,
+                                                      rank * q_heads, world * q_heads, counter, rank);
     return cuda_status(e, "gather launch");
   }
-  cudaError_t e = cudaLaunchKernelEx(&cfg, combine_gather_kernel<false>, static_cast<const float*>(lse_accum),
-                                     static_cast<const float*>(out_accum),
-                                     static_cast<const __nv_bfloat16*>(out_local), batch, q_heads,
-                                     partials ? num_splits : 1, peers, world, rank * q_heads, world * q_heads,
-                                     counter, rank);
+  cudaError_t e = launch_combine_gather<false>(cfg, w, la, oa, lo, batch, q_heads, splits, peers, world,
+                                               rank * q_heads, world * q_heads, counter, rank);
   if (e == cudaSuccess) {
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(32);
