@@ -131,9 +131,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap kmap_half,
                       const __grid_constant__ CUtensorMap vmap_half) {
-  // A split-KV combine launched after this grid with programmatic stream
-  // serialization may be scheduled now; it waits (griddepcontrol.wait) for
-  // this grid to complete before it reads the partials.
+  // The kernel after this grid on the stream, when launched with
+  // programmatic stream serialization (the split-KV combine, the next
+  // decode), may be scheduled now; it waits (griddepcontrol.wait) for this
+  // grid to complete before it touches global memory.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
@@ -150,37 +151,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int row = cta / p.kvh;
   const int head0 = kvhead * (p.qh / p.kvh) + hgroup * kN;
   const int group = min(kN, p.qh / p.kvh - hgroup * kN);  // this CTA's heads
-  const int len = p.lens[row];
-  const bool valid = len >= 1 && (long long)len <= (long long)p.table_stride * p.block_size;
-  const int n_tiles_total = valid ? (len + kTok - 1) / kTok : 0;
-  const int per_split = (n_tiles_total + p.num_splits - 1) / p.num_splits;
-  const int t0 = split * per_split;
-  const int t1 = min(t0 + per_split, n_tiles_total);
-  const int ntiles = max(0, t1 - t0);
-  const long long lse_base = (long long)row * p.qh * p.max_q;
-
-  if (ntiles == 0 || tile_addr + kTileBytes > raw_addr + kSmemBytes) {
-    if (ntiles != 0 && threadIdx.x == 0) record_error(kErrPrefillAlign);
-    for (int e = threadIdx.x; e < group * 128; e += blockDim.x) {
-      const int g = e >> 7, d = e & 127;
-      const long long rh = (long long)row * p.qh + head0 + g;
-      if (p.num_splits == 1) {
-        p.out[rh * 128 + d] = __float2bfloat16_rn(0.0f);
-        if (d == 0 && p.lse) p.lse[lse_base + (long long)(head0 + g) * p.max_q] = -INFINITY;
-      } else {
-        p.out_accum[((long long)split * p.rows * p.qh + rh) * 128 + d] = 0.0f;
-        if (d == 0) p.lse_accum[(long long)split * p.rows * p.qh + rh] = -INFINITY;
-      }
-    }
-    return;
-  }
-
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem_raw + kTmemSlotOff);
   float* exch = reinterpret_cast<float*>(smem_raw + kExchOff);  // [2][4][kN]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int* table = p.block_table + (long long)row * p.table_stride;
 
+  // Set-up that touches only this CTA's shared memory and TMEM: when the
+  // grid is launched as a programmatic dependent of the previous kernel on
+  // the stream, it overlaps that kernel's tail.
   if (threadIdx.x == 0) {
     for (int s = 0; s < kKStages; ++s) {
       mbar_init(&bars[kKFull + s], 1);
@@ -206,6 +184,44 @@ __global__ void __launch_bounds__(kThreads, 2)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  // The previous kernel has completed, its writes visible (this grid's
+  // inputs, and for split-KV the previous combine's reads of the partials
+  // this grid overwrites), before any global access below.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int len = p.lens[row];
+  const bool valid = len >= 1 && (long long)len <= (long long)p.table_stride * p.block_size;
+  const int n_tiles_total = valid ? (len + kTok - 1) / kTok : 0;
+  const int per_split = (n_tiles_total + p.num_splits - 1) / p.num_splits;
+  const int t0 = split * per_split;
+  const int t1 = min(t0 + per_split, n_tiles_total);
+  const int ntiles = max(0, t1 - t0);
+  const long long lse_base = (long long)row * p.qh * p.max_q;
+
+  if (ntiles == 0 || tile_addr + kTileBytes > raw_addr + kSmemBytes) {
+    if (ntiles != 0 && threadIdx.x == 0) record_error(kErrPrefillAlign);
+    for (int e = threadIdx.x; e < group * 128; e += blockDim.x) {
+      const int g = e >> 7, d = e & 127;
+      const long long rh = (long long)row * p.qh + head0 + g;
+      if (p.num_splits == 1) {
+        p.out[rh * 128 + d] = __float2bfloat16_rn(0.0f);
+        if (d == 0 && p.lse) p.lse[lse_base + (long long)(head0 + g) * p.max_q] = -INFINITY;
+      } else {
+        p.out_accum[((long long)split * p.rows * p.qh + rh) * 128 + d] = 0.0f;
+        if (d == 0) p.lse_accum[(long long)split * p.rows * p.qh + rh] = -INFINITY;
+      }
+    }
+    // nothing to decode: free the TMEM allocated above
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(*tmem_slot), "r"(kTmemCols)
+                   : "memory");
+    }
+    return;
+  }
+
+  const int* table = p.block_table + (long long)row * p.table_stride;
   if (warp >= 2) {
     // Q^T [16 heads][128 dims] (rows >= group zero) and the zero rows of P^T.
     const int t = threadIdx.x - 64;
@@ -494,8 +510,20 @@ cudaError_t launch_decode_mma(const DecodeParams& p, const CUtensorMap& kmap, co
   if (e != cudaSuccess) return e;
   const long long grid = (long long)p.rows * p.kvh * p.n_hgroups * p.num_splits;
   if (grid <= 0 || grid > 0x7fffffffLL) return cudaErrorInvalidValue;
-  decode_mma_kernel<<<unsigned(grid), kThreads, kSmemBytes, stream>>>(p, kmap, vmap, kmap_half, vmap_half);
-  return cudaGetLastError();
+  // Programmatic dependent of the kernel before it on the stream: barrier
+  // set-up and TMEM allocation overlap that kernel's tail; every global
+  // access waits (griddepcontrol.wait) for it to complete.
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_mma_kernel, p, kmap, vmap, kmap_half, vmap_half);
 }
 
 }  // namespace nvb
