@@ -98,15 +98,22 @@ __global__ void __launch_bounds__(combine_detail::kCombineThreads)
     const int set = counter ? int(step_epoch(0, counter) & 1u) : 0;
     for (int p = 0; p < world; ++p) *reinterpret_cast<uint2*>(peers.out[set][p] + dst) = packed;
   }
-  __threadfence_system();  // the stores are visible to the peers before this thread ends
+  if constexpr (!kBarrier) __threadfence_system();  // the stores are visible to the peers before this thread ends
   if constexpr (kBarrier) {
+    // One system-scope fence per CTA: the barrier orders every thread's peer
+    // stores before thread 0's fence, which orders them before its count (the
+    // pattern of a grid-wide barrier); the last CTA's release of its epoch
+    // flag then follows every CTA's stores. A fence in every thread costs
+    // ~4.5 us more per step (measured at 74 splits x 32 items).
     __shared__ int last;
     __syncthreads();
     unsigned int* done = counter + 1;
-    if (threadIdx.x == 0) last = atomicAdd(done, 1u) == unsigned(gridDim.x) - 1u;
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      last = atomicAdd(done, 1u) == unsigned(gridDim.x) - 1u;
+    }
     __syncthreads();
     if (!last || threadIdx.x >= 32) return;
-    __threadfence_system();
     const unsigned int epoch = step_epoch(0, counter);
     exchange_epoch(peers, world, rank, epoch, lane);
     __syncwarp();
