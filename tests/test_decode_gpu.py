@@ -261,6 +261,16 @@ def test_long_context_config5_shard(nvb, oracle):
     _check(nvb, oracle, case, splits, what="ctx 32768")
 
 
+@pytest.mark.parametrize("splits", [1, 7, 37, 74, 128])
+def test_shard_split_counts(nvb, oracle, splits):
+    # The config-5 shard of 8 GPUs in miniature: 4 ragged sequences x 1 kv head
+    # (8 query heads), ctx up to 8192, split 1 to 128 ways (the combine with 1,
+    # 2, 4 and 8 warps per item; 128 splits leave the short sequence's
+    # trailing splits without keys).
+    case = nvb.workloads.paged_case([8192, 8000, 7777, 129], q_heads=8, kv_heads=1, seed=31 + splits)
+    _check(nvb, oracle, case, splits, what=f"{splits} splits")
+
+
 def test_config3_full_size_sampled(nvb, oracle):
     # Full config 3 on the GPU; a sample of its sequences checked on the CPU.
     case = nvb.workloads.config3_decode()
