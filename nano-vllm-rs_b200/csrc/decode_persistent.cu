@@ -156,9 +156,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     decode_persistent_kernel(const DecodeParams p, int* sched, const __grid_constant__ CUtensorMap kmap,
                              const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap kmap_half,
                              const __grid_constant__ CUtensorMap vmap_half, const __grid_constant__ CUtensorMap qmap) {
-  // A split-KV combine launched after this grid with programmatic stream
-  // serialization may be scheduled now; it waits (griddepcontrol.wait) for
-  // this grid to complete before it reads the partials.
+  // The kernel after this grid on the stream, when launched with
+  // programmatic stream serialization (a split-KV combine), may be scheduled
+  // now; it waits (griddepcontrol.wait) for this grid to complete before it
+  // reads the partials.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
@@ -166,6 +167,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   unsigned char* tiles = smem_raw + (tile_addr - raw_addr);
   const uint32_t sbase = tile_addr;
   if (tile_addr + kTileBytes > raw_addr + kSmemBytes) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (threadIdx.x == 0) record_error(kErrPrefillAlign);
     return;
   }
@@ -224,6 +226,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched as a programmatic dependent of the previous kernel on the
+  // stream: the set-up above touches only this CTA's shared memory and TMEM
+  // and overlaps that kernel's tail. Wait for it to complete, its writes
+  // (the new tokens' K/V and queries, this stream's claim-counter reset)
+  // visible, before any global access.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 0) {
     // ------------------------------------------ item claims and producer
@@ -661,8 +669,17 @@ cudaError_t launch_decode_persistent(const DecodeParams& p, const CUtensorMap& k
   if (items <= 0 || items > 0x7fffffffLL) return cudaErrorInvalidValue;
   const int slots = __atomic_load_n(&resident[slot], __ATOMIC_ACQUIRE);
   const unsigned grid = unsigned(items < slots ? items : slots);
-  decode_persistent_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p, sched, kmap, vmap, kmap_half, vmap_half, qmap);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_persistent_kernel, p, sched, kmap, vmap, kmap_half, vmap_half, qmap);
 }
 
 }  // namespace nvb

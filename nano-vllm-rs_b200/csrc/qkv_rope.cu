@@ -35,6 +35,10 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(
     const int* __restrict__ slots, __nv_bfloat16* __restrict__ qout, __nv_bfloat16* __restrict__ kcache,
     __nv_bfloat16* __restrict__ vcache, int rows, int qheads, int kvheads, int block_size,
     int num_blocks, float eps, float theta, const float* __restrict__ rope_cache, int max_positions) {
+  // The decode launched after this kernel as a programmatic dependent may be
+  // scheduled now (its set-up overlaps this grid); it waits for this grid to
+  // complete before it reads the new tokens.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   constexpr int kDim = 128, kHalf = 64;
   const int lane = threadIdx.x & 31;
   const int heads = qheads + kvheads;
