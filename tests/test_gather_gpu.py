@@ -30,7 +30,9 @@ def _reference(nvb, case, splits):
     return out
 
 
-@pytest.mark.parametrize("splits", [1, 6])
+# 12 / 24 / 74 splits: the combine shared by 2 / 4 / 8 warps per item (74, the
+# config-5 shard of 8 GPUs, leaves the shortest sequence's last splits empty).
+@pytest.mark.parametrize("splits", [1, 6, 12, 24, 74])
 def test_gather_world1_matches_paged_fwd(nvb, splits):
     import importlib
 
@@ -58,7 +60,7 @@ def test_gather_world1_matches_paged_fwd(nvb, splits):
         nvb.peer_buffer_free(ptr)
 
 
-@pytest.mark.parametrize("splits", [1, 6])
+@pytest.mark.parametrize("splits", [1, 6, 74])
 def test_capturable_gather_world1_graph_replay(nvb, splits):
     """The capturable form: eager steps, then one captured step replayed
     three times; the device epoch picks the output set (odd steps set 1),
