@@ -340,6 +340,69 @@ def long_context_leg(nvb, W, dev, rank, world, stream, steps=50):
             "workload": "config5: 4 seqs x ctx 32768, 64q/8kv, kv-head sharded over the GPUs, split-KV per GPU"}
 
 
+def long_context_shard_leg(nvb, W, dev, of_gpus, steps):
+    """Rank 0's share of config 5 on `of_gpus` GPUs, run on this one GPU: the
+    per-rank shard (8 / N kv heads, their 64 / N query heads, 4 x 32768) with
+    the step a rank runs at N > 1 - split-KV decode, then the combine fused
+    with the gather and its epoch exchange - but over a world of one (the
+    exchange is with this rank itself: the kernels' cost without NVLink or
+    rank skew). Graph-replayed over KV sets rotated beyond L2, beside the
+    local decode + combine alone. A diagnostic for one process (so ncu can
+    capture it): no whole-job figure is claimed."""
+    import importlib
+
+    import torch
+
+    S = importlib.import_module("nano_vllm_rs_b200.sharding")
+    batch, ctx = 4, 32768
+    kv, q = 8 // of_gpus, 64 // of_gpus
+    shard = S.HeadShard(0, 1, kv_heads=kv, q_heads=q)
+    set_bytes = batch * ctx * kv * 512
+    nsets = max(2, -(-3 * 126 * 2**20 // set_bytes))
+    cases = [W.paged_case([ctx] * batch, q_heads=q, kv_heads=kv, seed=900 + i, device=dev) for i in range(nsets)]
+    c0 = cases[0]
+    kw = dict(batch=batch, block_size=256, table_stride=c0.table_stride, num_blocks=c0.num_blocks, max_k=ctx,
+              device=dev)
+    fused = S.KvHeadShardedDecode(nvb, shard, fused=True, **kw)
+    local = S.KvHeadShardedDecode(nvb, shard, fused=False, num_splits=fused.splits, **kw)
+    args = [(c.q, c.k, c.v, c.cu_q, c.kv_lens, c.block_table) for c in cases]
+    for a in args:
+        fused(*a)
+        local.local(*a)
+    torch.cuda.synchronize()
+    g_fused = [fused.capture(*a) for a in args]
+    g_local = []
+    for a in args:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            local.local(*a, check=False)
+        g_local.append(g)
+
+    def timed(fn):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    local_ms = timed(lambda i: g_local[i % nsets].replay())
+    fused_ms = timed(lambda i: fused.replay(g_fused[i % nsets]))
+    err = nvb.device_error()
+    del g_fused, g_local
+    fused.close()
+    if err:
+        raise RuntimeError(f"long-context shard step recorded device error {err}")
+    return {"emulates": f"rank 0 of config 5 on {of_gpus} GPUs (exchange over a world of one: no NVLink, no rank skew)",
+            "kv_heads": kv, "q_heads": q, "splits": fused.splits, "fused_step_ms": round(fused_ms, 5),
+            "local_step_ms": round(local_ms, 5), "gather_exchange_ms": round(fused_ms - local_ms, 5),
+            "local_gbs": round(set_bytes / (local_ms / 1e3) / 1e9, 1)}
+
+
 def engine_leg(nvb, dev, rank, world, runs=1, max_tokens=512):
     """the Qwen3-0.6B engine (28 layers, random weights
     N(0, 0.02)) generating for 256 requests with prompt ids uniform over the
@@ -419,6 +482,8 @@ def main():
     ap.add_argument("--e2e-split", type=str, default=None,
                     help="comma-separated chunk sizes in sequences (sum = batch); overrides --e2e-chunks")
     ap.add_argument("--no-long-context", action="store_true")
+    ap.add_argument("--long-context-shard", type=int, default=0, choices=[0, 1, 2, 4, 8],
+                    help="one GPU only: also time rank 0's share of config 5 on N GPUs (diagnostic)")
     ap.add_argument("--no-engine", action="store_true")
     ap.add_argument("--engine-runs", type=int, default=1, help="timed generate() calls of the config-4 engine leg")
     ap.add_argument("--engine-max-tokens", type=int, default=512,
@@ -738,6 +803,9 @@ def main():
     long_ctx = None
     if not args.no_long_context and 8 % world == 0:
         long_ctx = long_context_leg(nvb, W, dev, rank, world, stream)
+    shard_probe = None
+    if args.long_context_shard and world == 1:
+        shard_probe = long_context_shard_leg(nvb, W, dev, args.long_context_shard, max(args.steps, 3))
 
     # ---------------- config 4 engine, one replica per GPU
     engine = None
@@ -771,6 +839,7 @@ def main():
             "tok_s_note": "decode query tokens per second through one attention layer",
             "prefill": prefill,
             "long_context": long_ctx,
+            **({"long_context_shard": shard_probe} if shard_probe else {}),
             "engine": engine,
             "e2e": None if e2e_value is None else {
                 "value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
