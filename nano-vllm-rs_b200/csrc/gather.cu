@@ -37,11 +37,15 @@ __device__ __forceinline__ unsigned int step_epoch(unsigned int host_epoch, cons
 }
 
 // Lanes p < world: signal `epoch` into rank p's slot `rank`, then wait (bounded)
-// until rank p's epoch has arrived in this rank's slot p.
+// until rank p's epoch has arrived in this rank's slot p. kFence: a full
+// system-scope fence before the releasing store (the host-epoch barrier
+// kernel, whose ordering with the combine grid comes from griddepcontrol.wait);
+// without it the store's own release semantics order what precedes it.
+template <bool kFence>
 __device__ __forceinline__ void exchange_epoch(const PeerPtrs& peers, int world, int rank, unsigned int epoch,
                                                int lane) {
   if (lane >= world) return;
-  __threadfence_system();
+  if constexpr (kFence) __threadfence_system();
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.flag[lane] + rank), "r"(epoch) : "memory");
   const unsigned int* mine = peers.flag[rank] + lane;
   const long long start = clock64();
@@ -62,9 +66,20 @@ __device__ __forceinline__ void exchange_epoch(const PeerPtrs& peers, int world,
 // splits == 1: copies the local decode output. The result goes to every rank
 // at head offset head_offset (= rank * qh local).
 // kBarrier (the counter form): the CTA that finishes last (a done count in
-// the rank's flag slot world + 1; every CTA fences its peer stores at system
-// scope before counting) runs the epoch exchange itself, advances the device
-// epoch and resets the count, so the step needs no separate barrier launch.
+// the rank's flag slot world + 1) runs the epoch exchange itself, advances
+// the device epoch and resets the count, so the step needs no separate
+// barrier launch.
+//
+// Ordering of the counter form, in the PTX memory model (causality order is
+// transitive; each synchronising pair needs only a scope that holds both
+// threads): a CTA's peer stores precede its thread 0's count by bar.sync; the
+// count is an acquire-release RMW at GPU scope, and every CTA that counts runs
+// on this GPU, so each count synchronises with the last CTA's; that CTA's
+// bar.sync then orders them before each lane's st.release.sys of the epoch
+// flag, which is cumulative, and a peer that acquires the flag at system scope
+// sees every store of the grid. A system-scope fence in each CTA instead
+// measured ~4 us per step (it waits for the CTA's NVLink stores to complete),
+// the GPU-scope count ~0.9 us.
 template <bool kBarrier, int W>
 __global__ void __launch_bounds__(combine_detail::kCombineThreads)
     combine_gather_kernel(const float* __restrict__ lse_accum, const float* __restrict__ out_accum,
@@ -75,6 +90,9 @@ __global__ void __launch_bounds__(combine_detail::kCombineThreads)
   // now, and this grid waits for the decode to complete before reading.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The step's epoch (counter form), loaded once: its latency hides under the
+  // combine's loads, and the last CTA reuses it for the exchange.
+  const unsigned int epoch = counter ? step_epoch(0, counter) : 0u;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = warp % W;
   const long long item = (long long)blockIdx.x * (combine_detail::kCombineThreads / 32 / W) + warp / W;
   const bool live = item < (long long)rows * qh;
@@ -95,27 +113,22 @@ __global__ void __launch_bounds__(combine_detail::kCombineThreads)
     }
     const long long row = item / qh, h = item - row * qh;
     const long long dst = (row * qh_total + head_offset + h) * 128 + lane * 4;
-    const int set = counter ? int(step_epoch(0, counter) & 1u) : 0;
+    const int set = int(epoch & 1u);
     for (int p = 0; p < world; ++p) *reinterpret_cast<uint2*>(peers.out[set][p] + dst) = packed;
   }
   if constexpr (!kBarrier) __threadfence_system();  // the stores are visible to the peers before this thread ends
   if constexpr (kBarrier) {
-    // One system-scope fence per CTA: the barrier orders every thread's peer
-    // stores before thread 0's fence, which orders them before its count (the
-    // pattern of a grid-wide barrier); the last CTA's release of its epoch
-    // flag then follows every CTA's stores. A fence in every thread costs
-    // ~4.5 us more per step (measured at 74 splits x 32 items).
     __shared__ int last;
     __syncthreads();
     unsigned int* done = counter + 1;
     if (threadIdx.x == 0) {
-      __threadfence_system();
-      last = atomicAdd(done, 1u) == unsigned(gridDim.x) - 1u;
+      unsigned int prev;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(done) : "memory");
+      last = prev == unsigned(gridDim.x) - 1u;
     }
     __syncthreads();
     if (!last || threadIdx.x >= 32) return;
-    const unsigned int epoch = step_epoch(0, counter);
-    exchange_epoch(peers, world, rank, epoch, lane);
+    exchange_epoch<false>(peers, world, rank, epoch, lane);
     __syncwarp();
     if (lane == 0) {
       *done = 0u;
@@ -134,7 +147,7 @@ __global__ void gather_barrier_kernel(PeerPtrs peers, int world, int rank, unsig
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x;
   const unsigned int epoch = step_epoch(host_epoch, counter);
-  exchange_epoch(peers, world, rank, epoch, lane);
+  exchange_epoch<true>(peers, world, rank, epoch, lane);
   __syncwarp();
   if (counter && lane == 0) *counter = epoch;
 }
