@@ -25,11 +25,16 @@
 // partial row sums that are reduced once at the end. The CUDA cores do a few
 // instructions per KV token, so the kernel stays HBM-bound at any SM clock.
 //
-// Warp roles: warp 0 streams 128-token K and V tiles (32 KB each; 2-stage K
-// ring, 1-stage V ring) with 3-D TMA, warp 1 owns TMEM and issues the MMAs,
+// Warp roles: warp 0 streams 128-token K and V tiles (32 KB each) with 3-D
+// TMA into one 3-slot ring that K and V share, in the order K0 V0 K1 V1 ...
+// (both tiles have the same shared-memory layout; only the MMA descriptors
+// differ), so V_{j+1} is loaded as soon as S_j frees its slot rather than
+// after PV_j; warp 1 owns TMEM and issues the MMAs,
 // warps 2..5 run the softmax and the epilogue. 105 KB of shared memory and 64
 // TMEM columns per CTA allow two CTAs per SM. Every mbarrier is waited on
-// every phase, in order, by each of its waiters.
+// every phase, in order, by each of its waiters, except the softmax's wait
+// for a V tile, taken only on tiles with masked tokens; that slot cannot run
+// two phases ahead of it, since its next load needs this tile's PV.
 #include "internal.cuh"
 
 namespace nvb {
@@ -38,8 +43,7 @@ namespace decode_mma_detail {
 
 constexpr int kTok = 128;                 // tokens per tile (MMA M)
 constexpr int kN = 16;                    // padded heads per CTA (MMA N)
-constexpr int kKStages = 2;
-constexpr int kVStages = 1;
+constexpr int kStages = 3;                // ring slots shared by K and V tiles
 constexpr int kHalf = kTok * 128;         // 128 rows x 64 BF16
 constexpr int kKVBytes = 2 * kHalf;       // 32 KB tile
 constexpr int kNHalf = kN * 128;          // 16 rows x 64 BF16
@@ -52,16 +56,16 @@ constexpr float kRescaleLog2 = 8.0f;
 
 // kXch: per-tile exchange of the four softmax warps' maxima (two barriers,
 // alternating by tile parity, so each is waited on every phase in order).
-enum Bar { kKFull = 0, kKEmpty = kKFull + kKStages, kVFull = kKEmpty + kKStages, kVEmpty = kVFull + kVStages,
-           kSFull = kVEmpty + kVStages, kSFree = kSFull + 2, kPFull = kSFree + 2, kODone = kPFull + 1,
-           kXch = kODone + 1, kNumBars = kXch + 2 };
+enum Bar { kFull = 0, kEmpty = kFull + kStages, kSFull = kEmpty + kStages, kSFree = kSFull + 2,
+           kPFull = kSFree + 2, kODone = kPFull + 1, kXch = kODone + 1, kNumBars = kXch + 2 };
 constexpr int kTmemSlotOff = kNumBars * 8;
 constexpr int kExchOff = kTmemSlotOff + 16;         // float [2][4 warps][16] max exchange
 constexpr int kHeadBytes = kExchOff + 2 * 4 * kN * 4;
 static_assert(kHeadBytes <= 1024, "barrier block must fit below the first 1 KB boundary");
-constexpr int kKOff = 0;
-constexpr int kVOff = kKOff + kKStages * kKVBytes;
-constexpr int kQOff = kVOff + kVStages * kKVBytes;
+// Ring load n (K of tile n / 2 when n is even, its V when odd) uses slot
+// n % kStages.
+constexpr int kRingOff = 0;
+constexpr int kQOff = kRingOff + kStages * kKVBytes;
 constexpr int kPOff = kQOff + kNBytes;
 constexpr int kTileBytes = kPOff + kNBytes;
 constexpr int kSmemBytes = 1024 + kTileBytes;
@@ -160,13 +164,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   // grid is launched as a programmatic dependent of the previous kernel on
   // the stream, it overlaps that kernel's tail.
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kKStages; ++s) {
-      mbar_init(&bars[kKFull + s], 1);
-      mbar_init(&bars[kKEmpty + s], 1);
-    }
-    for (int s = 0; s < kVStages; ++s) {
-      mbar_init(&bars[kVFull + s], 1);
-      mbar_init(&bars[kVEmpty + s], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars[kFull + s], 1);
+      mbar_init(&bars[kEmpty + s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[kSFull + s], 1);
@@ -252,38 +252,30 @@ __global__ void __launch_bounds__(kThreads, 2)
       tma_prefetch_desc(&kmap_half);
       tma_prefetch_desc(&vmap_half);
       const uint64_t policy = policy_evict_first();
-      for (int i = 0; i < ntiles; ++i) {
-        const int token0 = (t0 + i) * kTok;
+      for (int n = 0; n < 2 * ntiles; ++n) {
+        const int token0 = (t0 + (n >> 1)) * kTok;
         const int logical = token0 / p.block_size;
         const int page = table[logical];
         const bool ok = page >= 0 && page < p.num_blocks;
         const int trow = ok ? page * p.block_size + (token0 - logical * p.block_size) : 0;
         // A sequence's last tile with at most 64 live tokens loads only its
-        // first 64 rows (the rest of the stage is stale and masked: scores
+        // first 64 rows (the rest of the slot is stale and masked: scores
         // of tokens past the length are dropped and their V rows zeroed),
         // which halves the bytes read past the end of ragged contexts.
         const bool half = len - token0 <= kTok / 2;
-        const CUtensorMap* km = half ? &kmap_half : &kmap;
-        const CUtensorMap* vm = half ? &vmap_half : &vmap;
+        const CUtensorMap* m = (n & 1) ? (half ? &vmap_half : &vmap) : (half ? &kmap_half : &kmap);
         const uint32_t tile_bytes = half ? kKVBytes / 2 : kKVBytes;
-        const int ks = i % kKStages, vs = i % kVStages;
-        if (i >= kKStages && !mbar_wait(&bars[kKEmpty + ks], ((i / kKStages) + 1) & 1, kErrDecodeEmptyWait)) break;
+        const int slot = n % kStages;
+        // The slot's previous load (n - kStages) is released by the MMA that
+        // read it: S of a K tile, PV of a V tile.
+        if (n >= kStages && !mbar_wait(&bars[kEmpty + slot], ((n / kStages) + 1) & 1, kErrDecodeEmptyWait)) break;
         if (ok) {
-          unsigned char* kd = tiles + kKOff + ks * kKVBytes;
-          mbar_arrive_expect_tx(&bars[kKFull + ks], tile_bytes);
-          tma_load_3d_hint(kd, km, &bars[kKFull + ks], 0, kvhead, trow, policy);
-          tma_load_3d_hint(kd + kHalf, km, &bars[kKFull + ks], 64, kvhead, trow, policy);
+          unsigned char* d = tiles + kRingOff + slot * kKVBytes;
+          mbar_arrive_expect_tx(&bars[kFull + slot], tile_bytes);
+          tma_load_3d_hint(d, m, &bars[kFull + slot], 0, kvhead, trow, policy);
+          tma_load_3d_hint(d + kHalf, m, &bars[kFull + slot], 64, kvhead, trow, policy);
         } else {
-          mbar_arrive(&bars[kKFull + ks]);
-        }
-        if (i >= kVStages && !mbar_wait(&bars[kVEmpty + vs], ((i / kVStages) + 1) & 1, kErrDecodeEmptyWait)) break;
-        if (ok) {
-          unsigned char* vd = tiles + kVOff + vs * kKVBytes;
-          mbar_arrive_expect_tx(&bars[kVFull + vs], tile_bytes);
-          tma_load_3d_hint(vd, vm, &bars[kVFull + vs], 0, kvhead, trow, policy);
-          tma_load_3d_hint(vd + kHalf, vm, &bars[kVFull + vs], 64, kvhead, trow, policy);
-        } else {
-          mbar_arrive(&bars[kVFull + vs]);
+          mbar_arrive(&bars[kFull + slot]);
         }
       }
     }
@@ -293,12 +285,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       bool alive = true;
       const uint32_t q_addr = sbase + kQOff, p_addr = sbase + kPOff;
       auto issue_pv = [&](int t) {
-        const int vs = t % kVStages;
+        const int n = 2 * t + 1, slot = n % kStages;
         alive = alive && mbar_wait(&bars[kPFull], t & 1, kErrDecodeFullWait);
-        alive = alive && mbar_wait(&bars[kVFull + vs], (t / kVStages) & 1, kErrDecodeFullWait);
+        alive = alive && mbar_wait(&bars[kFull + slot], (n / kStages) & 1, kErrDecodeFullWait);
         if (!alive) return;
         tc_fence_after();
-        const uint32_t v_addr = sbase + kVOff + vs * kKVBytes;
+        const uint32_t v_addr = sbase + kRingOff + slot * kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < kTok / 16; ++kk) {
           // A = V^T, MN-major: 64-dim halves kHalf apart, 8-token groups 1 KB apart
@@ -306,23 +298,23 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint64_t b = sw128_desc(p_addr + (kk >> 2) * kNHalf + (kk & 3) * 32, 16, 1024);
           umma(tmem + kOCol, a, b, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bars[kVEmpty + vs]);
+        umma_commit(&bars[kEmpty + slot]);
         umma_commit(&bars[kODone]);
       };
       for (int j = 0; j < ntiles && alive; ++j) {
-        const int ks = j % kKStages, sb = j & 1;
-        alive = mbar_wait(&bars[kKFull + ks], (j / kKStages) & 1, kErrDecodeFullWait);
+        const int n = 2 * j, slot = n % kStages, sb = j & 1;
+        alive = mbar_wait(&bars[kFull + slot], (n / kStages) & 1, kErrDecodeFullWait);
         if (alive && j >= 2) alive = mbar_wait(&bars[kSFree + sb], ((j >> 1) + 1) & 1, kErrDecodeFullWait);
         if (!alive) break;
         tc_fence_after();
-        const uint32_t k_addr = sbase + kKOff + ks * kKVBytes;
+        const uint32_t k_addr = sbase + kRingOff + slot * kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t a = sw128_desc(k_addr + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
           const uint64_t b = sw128_desc(q_addr + (kk >> 2) * kNHalf + (kk & 3) * 32, 16, 1024);
           umma(tmem + sb * kN, a, b, kIdescS, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bars[kKEmpty + ks]);
+        umma_commit(&bars[kEmpty + slot]);
         umma_commit(&bars[kSFull + sb]);
         if (j >= 1) issue_pv(j - 1);
       }
@@ -407,16 +399,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc_fence_after();
       }
       // V rows of tokens that are not real keys are zeroed: P = 0 must never
-      // meet a non-finite cache value. PV_{j-1} done means V_{j-1} was
-      // consumed, so this vfull wait is for V_j itself.
+      // meet a non-finite cache value. The wait is for V_j's load itself:
+      // the slot's next load (K_{j+2}) needs PV_j, which needs this P_j.
       if (__any_sync(0xffffffffu, !live)) {
-        const int vs = j % kVStages;
-        if (!mbar_wait(&bars[kVFull + vs], (j / kVStages) & 1, kErrDecodeFullWait)) {
+        const int n = 2 * j + 1, slot = n % kStages;
+        if (!mbar_wait(&bars[kFull + slot], (n / kStages) & 1, kErrDecodeFullWait)) {
           alive = false;
           break;
         }
         if (!live) {
-          const uint32_t vrow = sbase + kVOff + vs * kKVBytes + t * 128;
+          const uint32_t vrow = sbase + kRingOff + slot * kKVBytes + t * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             st_shared_zero16(vrow + c * 16);
