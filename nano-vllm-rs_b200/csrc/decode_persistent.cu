@@ -17,10 +17,13 @@
 // keep.
 //
 // Warp roles: warp 0 claims items and streams each item's Q^T and K/V tiles
-// (2-stage K ring, 1-stage V ring, 32 KB tiles) with 3-D TMA, warp 1 owns TMEM
-// and issues the MMAs, warps 2..5 run the softmax and the epilogue. Every
-// mbarrier is waited on every phase, in order, by each of its waiters; phases
-// count tiles (or items) over the CTA's whole item stream. The softmax warps'
+// (32 KB tiles, K and V sharing one 3-slot ring in the order K0 V0 K1 V1 ...,
+// as the one-CTA-per-item kernel does) with 3-D TMA, warp 1 owns TMEM and
+// issues the MMAs, warps 2..5 run the softmax and the epilogue. Every
+// mbarrier is waited on every phase, in order, by each of its waiters (except
+// the softmax's wait for a V tile, taken only on tiles with masked tokens: its
+// slot's next load needs this tile's PV, so it cannot run two phases ahead);
+// phases count tiles (or items) over the CTA's whole item stream. The softmax warps'
 // waits are warp-uniform and bounded, and no role waits at a barrier without
 // a time limit.
 #include <mutex>
@@ -33,8 +36,7 @@ namespace decode_persistent_detail {
 
 constexpr int kTok = 128;                 // tokens per tile (MMA M)
 constexpr int kN = 16;                    // padded heads per CTA (MMA N)
-constexpr int kKStages = 2;
-constexpr int kVStages = 1;
+constexpr int kStages = 3;                // ring slots shared by K and V tiles
 constexpr int kHalf = kTok * 128;         // 128 rows x 64 BF16
 constexpr int kKVBytes = 2 * kHalf;       // 32 KB tile
 constexpr int kNHalf = kN * 128;          // 16 rows x 64 BF16
@@ -49,8 +51,8 @@ constexpr float kRescaleLog2 = 8.0f;
 // alternating by tile parity, so each is waited on every phase in order).
 // kItemFull / kItemEmpty: the two-slot item ring; kQFull / kQEmpty: the two
 // Q^T buffers, used by items in turn; kLex: the epilogue's row-sum exchange.
-enum Bar { kKFull = 0, kKEmpty = kKFull + kKStages, kVFull = kKEmpty + kKStages, kVEmpty = kVFull + kVStages,
-           kSFull = kVEmpty + kVStages, kSFree = kSFull + 2, kPFull = kSFree + 2, kODone = kPFull + 1,
+enum Bar { kFull = 0, kEmpty = kFull + kStages, kSFull = kEmpty + kStages, kSFree = kSFull + 2,
+           kPFull = kSFree + 2, kODone = kPFull + 1,
            kXch = kODone + 1, kItemFull = kXch + 2, kItemEmpty = kItemFull + 2, kQFull = kItemEmpty + 2,
            kQEmpty = kQFull + 2, kLex = kQEmpty + 2, kNumBars = kLex + 1 };
 constexpr int kTmemSlotOff = kNumBars * 8;
@@ -59,9 +61,10 @@ constexpr int kLexOff = kExchOff + 2 * 4 * kN * 4;  // float [4 warps][16] row s
 constexpr int kRingOff = kLexOff + 4 * kN * 4;      // Item [2]
 constexpr int kHeadBytes = kRingOff + 2 * 28;  // sizeof(Item) == 28, checked below
 static_assert(kHeadBytes <= 1024, "barrier block must fit below the first 1 KB boundary");
-constexpr int kKOff = 0;
-constexpr int kVOff = kKOff + kKStages * kKVBytes;
-constexpr int kQOff = kVOff + kVStages * kKVBytes;
+// Tile load n (K of the CTA's tile n / 2 when n is even, its V when odd)
+// uses slot n % kStages.
+constexpr int kSlotOff = 0;
+constexpr int kQOff = kSlotOff + kStages * kKVBytes;
 constexpr int kPOff = kQOff + kNBytes;
 constexpr int kTileBytes = kPOff + kNBytes;
 constexpr int kSmemBytes = 1024 + kTileBytes;
@@ -182,13 +185,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kKStages; ++s) {
-      mbar_init(&bars[kKFull + s], 1);
-      mbar_init(&bars[kKEmpty + s], 1);
-    }
-    for (int s = 0; s < kVStages; ++s) {
-      mbar_init(&bars[kVFull + s], 1);
-      mbar_init(&bars[kVEmpty + s], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars[kFull + s], 1);
+      mbar_init(&bars[kEmpty + s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[kSFull + s], 1);
@@ -289,34 +288,26 @@ __global__ void __launch_bounds__(kThreads, 2)
           const int trow = ok ? page * p.block_size + (token0 - logical * p.block_size) : 0;
           // A sequence's last tile with at most 64 live tokens loads 64 rows.
           const bool half = it.len - token0 <= kTok / 2;
-          const CUtensorMap* km = half ? &kmap_half : &kmap;
-          const CUtensorMap* vm = half ? &vmap_half : &vmap;
           const uint32_t tile_bytes = half ? kKVBytes / 2 : kKVBytes;
-          const int ks = g % kKStages, vs = g % kVStages;
-          if (g >= kKStages && !mbar_wait(&bars[kKEmpty + ks], ((g / kKStages) + 1) & 1, kErrDecodeEmptyWait)) {
-            alive = false;
-            break;
+          // K then V of the tile; each slot's previous load (n - kStages) is
+          // released by the MMA that read it (S of a K tile, PV of a V tile).
+          for (int n = 2 * g; n <= 2 * g + 1; ++n) {
+            const CUtensorMap* m = (n & 1) ? (half ? &vmap_half : &vmap) : (half ? &kmap_half : &kmap);
+            const int slot = n % kStages;
+            if (n >= kStages && !mbar_wait(&bars[kEmpty + slot], ((n / kStages) + 1) & 1, kErrDecodeEmptyWait)) {
+              alive = false;
+              break;
+            }
+            if (ok) {
+              unsigned char* d = tiles + kSlotOff + slot * kKVBytes;
+              mbar_arrive_expect_tx(&bars[kFull + slot], tile_bytes);
+              tma_load_3d_hint(d, m, &bars[kFull + slot], 0, it.kvhead, trow, policy);
+              tma_load_3d_hint(d + kHalf, m, &bars[kFull + slot], 64, it.kvhead, trow, policy);
+            } else {
+              mbar_arrive(&bars[kFull + slot]);
+            }
           }
-          if (ok) {
-            unsigned char* kd = tiles + kKOff + ks * kKVBytes;
-            mbar_arrive_expect_tx(&bars[kKFull + ks], tile_bytes);
-            tma_load_3d_hint(kd, km, &bars[kKFull + ks], 0, it.kvhead, trow, policy);
-            tma_load_3d_hint(kd + kHalf, km, &bars[kKFull + ks], 64, it.kvhead, trow, policy);
-          } else {
-            mbar_arrive(&bars[kKFull + ks]);
-          }
-          if (g >= kVStages && !mbar_wait(&bars[kVEmpty + vs], ((g / kVStages) + 1) & 1, kErrDecodeEmptyWait)) {
-            alive = false;
-            break;
-          }
-          if (ok) {
-            unsigned char* vd = tiles + kVOff + vs * kKVBytes;
-            mbar_arrive_expect_tx(&bars[kVFull + vs], tile_bytes);
-            tma_load_3d_hint(vd, vm, &bars[kVFull + vs], 0, it.kvhead, trow, policy);
-            tma_load_3d_hint(vd + kHalf, vm, &bars[kVFull + vs], 64, it.kvhead, trow, policy);
-          } else {
-            mbar_arrive(&bars[kVFull + vs]);
-          }
+          if (!alive) break;
         }
         if (!alive) break;
       }
@@ -328,12 +319,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t p_addr = sbase + kPOff;
       // PV of global tile g; `first` starts the item's accumulator.
       auto issue_pv = [&](int g, bool first) {
-        const int vs = g % kVStages;
+        const int n = 2 * g + 1, slot = n % kStages;
         alive = alive && mbar_wait(&bars[kPFull], g & 1, kErrDecodeFullWait);
-        alive = alive && mbar_wait(&bars[kVFull + vs], (g / kVStages) & 1, kErrDecodeFullWait);
+        alive = alive && mbar_wait(&bars[kFull + slot], (n / kStages) & 1, kErrDecodeFullWait);
         if (!alive) return;
         tc_fence_after();
-        const uint32_t v_addr = sbase + kVOff + vs * kKVBytes;
+        const uint32_t v_addr = sbase + kSlotOff + slot * kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < kTok / 16; ++kk) {
           // A = V^T, MN-major: 64-dim halves kHalf apart, 8-token groups 1 KB apart
@@ -341,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint64_t b = sw128_desc(p_addr + (kk >> 2) * kNHalf + (kk & 3) * 32, 16, 1024);
           umma(tmem + kOCol, a, b, kIdescPV, (!first || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bars[kVEmpty + vs]);
+        umma_commit(&bars[kEmpty + slot]);
         umma_commit(&bars[kODone]);
       };
       int g = 0, ni = 0;
@@ -356,19 +347,19 @@ __global__ void __launch_bounds__(kThreads, 2)
         ++ni;
         const uint32_t q_addr = sbase + kQOff;
         for (int j = 0; j < it.ntiles && alive; ++j, ++g) {
-          const int ks = g % kKStages, sb = g & 1;
-          alive = mbar_wait(&bars[kKFull + ks], (g / kKStages) & 1, kErrDecodeFullWait);
+          const int n = 2 * g, slot = n % kStages, sb = g & 1;
+          alive = mbar_wait(&bars[kFull + slot], (n / kStages) & 1, kErrDecodeFullWait);
           if (alive && g >= 2) alive = mbar_wait(&bars[kSFree + sb], ((g >> 1) + 1) & 1, kErrDecodeFullWait);
           if (!alive) break;
           tc_fence_after();
-          const uint32_t k_addr = sbase + kKOff + ks * kKVBytes;
+          const uint32_t k_addr = sbase + kSlotOff + slot * kKVBytes;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t a = sw128_desc(k_addr + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
             const uint64_t b = sw128_desc(q_addr + (kk >> 2) * kNHalf + (kk & 3) * 32, 16, 1024);
             umma(tmem + sb * kN, a, b, kIdescS, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&bars[kKEmpty + ks]);
+          umma_commit(&bars[kEmpty + slot]);
           umma_commit(&bars[kSFull + sb]);
           if (j == it.ntiles - 1) umma_commit(&bars[kQEmpty]);
           if (j >= 1) issue_pv(g - 1, j == 1);
@@ -489,17 +480,17 @@ __global__ void __launch_bounds__(kThreads, 2)
           tc_fence_after();
         }
         // V rows of tokens that are not real keys are zeroed: P = 0 must
-        // never meet a non-finite cache value. The previous PV is complete,
-        // so the V stage holds this tile's V or is still being filled with
-        // it: this wait is for V of tile g itself.
+        // never meet a non-finite cache value. The wait is for V of tile g
+        // itself: the slot's next load (K of tile g + 2) needs PV of tile g,
+        // which needs this P.
         if (__any_sync(0xffffffffu, !live)) {
-          const int vs = g % kVStages;
-          if (!wwait(&bars[kVFull + vs], (g / kVStages) & 1)) {
+          const int n = 2 * g + 1, slot = n % kStages;
+          if (!wwait(&bars[kFull + slot], (n / kStages) & 1)) {
             alive = false;
             break;
           }
           if (!live) {
-            const uint32_t vrow = sbase + kVOff + vs * kKVBytes + t * 128;
+            const uint32_t vrow = sbase + kSlotOff + slot * kKVBytes + t * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
               st_shared_zero16(vrow + c * 16);
