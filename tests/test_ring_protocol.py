@@ -1,0 +1,434 @@
+"""A model check of the decode kernels' mbarrier protocol (CPU only).
+
+csrc/decode_mma.cu and csrc/decode_persistent.cu stream K and V tiles
+through one ring of kStages shared-memory slots (load n: K of tile n / 2
+when n is even, its V when odd, in slot n % kStages), and coordinate a TMA
+producer, an MMA-issuing thread, the tensor pipe and the softmax warps with
+mbarriers waited on by phase parity. This test restates each role's loop as
+a Python generator, with every wait's parity computed by the same formula as
+the CUDA source, and runs them under a random scheduler with TMA loads that
+land in any order and tensor-core operations that complete in issue order.
+
+It checks, over random tile counts, masked tiles, item streams and ring
+depths:
+  * no deadlock;
+  * every parity formula names the phase the waiter means (parity ==
+    intended phase & 1), and no barrier ever runs two phases ahead of a
+    waiter that has not yet passed its wait (a parity wait would alias);
+  * no slot is reloaded before the MMA that reads it has run, every MMA
+    reads the load it expects after it landed, the softmax zeroes V rows only
+    of the tile's own landed V, P and S buffers are rewritten only after
+    their readers, O is rescaled only between two tiles' PVs, and an item's
+    first PV (which restarts O) runs only after the previous item's epilogue
+    read O.
+
+The four softmax warps act in lockstep on every barrier they share, so they
+are one actor here (arrival counts 4 -> 1, the item ring's 5 -> 2).
+"""
+import random
+
+import pytest
+
+
+class Bar:
+    def __init__(self, name, count):
+        self.name, self.count, self.pending, self.done = name, count, count, 0
+
+    def __repr__(self):
+        return f"{self.name}(done={self.done}, pending={self.pending}/{self.count})"
+
+
+class Sim:
+    def __init__(self, seed, stages):
+        self.rng = random.Random(seed)
+        self.S = stages
+        self.bars = {}
+        self.waiting = {}  # actor -> (bar, k)
+        self.loads = []  # in-flight TMA loads: (callback)
+        self.tq = []  # tensor pipe queue, in issue order
+        # data state
+        self.slot_load = [None] * stages
+        self.slot_ready = [False] * stages
+        self.consumed = set()
+        self.s_buf = [None, None]
+        self.s_read = set()
+        self.p_buf = None
+        self.pv_done = -1
+        self.q_item = None
+        self.q_ready = False
+        self.s_issued_item = {}  # tile -> item
+        self.tile_item = {}
+        self.first_tile = {}  # item -> first global tile
+        self.last_tile = {}
+        self.epilogue_done = set()
+        self.s_done_tiles = set()
+
+    def bar(self, name, count=1):
+        if name not in self.bars:
+            self.bars[name] = Bar(name, count)
+        return self.bars[name]
+
+    def arrive(self, name):
+        b = self.bars[name]
+        b.pending -= 1
+        assert b.pending >= 0, b
+        if b.pending == 0:
+            b.done += 1
+            b.pending = b.count
+            for actor, (wb, k) in self.waiting.items():
+                assert not (wb is b and b.done > k + 1), f"{b} ran two phases past a waiter of phase {k} ({actor})"
+
+    # a wait instruction yielded by an actor
+    @staticmethod
+    def wait(name, parity, k):
+        assert parity == (k & 1), f"parity formula {parity} names another phase than {k} on {name}"
+        return ("wait", name, k)
+
+    def run(self, actors):
+        live = {a: g for a, g in actors.items()}
+        instr = {}
+        for a, g in live.items():
+            instr[a] = next(g, None)
+        done_actors = {a for a, i in instr.items() if i is None}
+
+        def ready(a):
+            i = instr[a]
+            if i is None:
+                return False
+            if i[0] == "wait":
+                b = self.bars[i[1]]
+                return b.done >= i[2] + 1
+            if i[0] == "tensor":
+                return bool(self.tq)
+            return True
+
+        steps = 0
+        while True:
+            steps += 1
+            assert steps < 200000, "simulation did not finish"
+            for a, i in instr.items():
+                if i is not None and i[0] == "wait":
+                    b = self.bars[i[1]]
+                    assert b.done <= i[2] + 1, f"{a} waits for phase {i[2]} of {b}: parity would alias"
+                    self.waiting[a] = (b, i[2])
+                else:
+                    self.waiting.pop(a, None)
+            choices = [("actor", a) for a in instr if ready(a)] + [("load", j) for j in range(len(self.loads))]
+            if not choices:
+                unfinished = [a for a, i in instr.items() if i is not None and a != "tensor"]
+                if not unfinished and not self.tq:
+                    return
+                raise AssertionError(f"deadlock: {[(a, instr[a]) for a in unfinished]} bars={list(self.bars.values())}")
+            kind, x = self.rng.choice(choices)
+            if kind == "load":
+                cb = self.loads.pop(x)
+                cb()
+                continue
+            try:
+                instr[x] = next(live[x])
+            except StopIteration:
+                instr[x] = None
+
+    # ---------------------------------------------------------------- events
+    def issue_load(self, n, ok):
+        s = n % self.S
+        prev = self.slot_load[s]
+        assert prev is None or (prev == n - self.S and prev in self.consumed), \
+            f"load {n} overwrites slot {s} holding load {prev} before its MMA ran"
+        self.slot_load[s], self.slot_ready[s] = n, False
+
+        def land():
+            assert self.slot_load[s] == n
+            self.slot_ready[s] = True
+            self.arrive(f"Full{s}")
+
+        if ok:
+            self.loads.append(land)
+        else:  # invalid page: the producer arrives without a copy (stale slot, masked)
+            land()
+
+    def read_slot(self, n):
+        s = n % self.S
+        assert self.slot_load[s] == n and self.slot_ready[s], f"MMA reads load {n}, slot {s} holds {self.slot_load[s]}"
+        self.consumed.add(n)
+
+    def tensor(self):
+        while True:
+            yield ("tensor",)
+            op = self.tq.pop(0)
+            if op[0] == "S":
+                _, g, item = op
+                assert self.q_item == item and self.q_ready, f"S of tile {g} (item {item}) without its Q"
+                self.read_slot(2 * g)
+                sb = g & 1
+                assert g < 2 or (g - 2) in self.s_read, f"S of tile {g} overwrites S of tile {g - 2} before it was read"
+                self.s_buf[sb] = g
+                self.s_done_tiles.add(g)
+            elif op[0] == "PV":
+                _, g = op
+                self.read_slot(2 * g + 1)
+                assert self.p_buf == g, f"PV of tile {g} reads P of tile {self.p_buf}"
+                assert self.pv_done == g - 1, f"PV of tile {g} after PV of tile {self.pv_done}"
+                item = self.tile_item[g]
+                if self.first_tile[item] == g:  # restarts O: the previous item's epilogue must have read it
+                    prev = [i for i in self.last_tile if self.last_tile[i] < g]
+                    if prev:
+                        assert max(prev, key=lambda i: self.last_tile[i]) in self.epilogue_done, \
+                            f"item {item}'s first PV overwrites O before the previous epilogue read it"
+                self.pv_done = g
+            elif op[0] == "commit":
+                self.arrive(op[1])
+            elif op[0] == "qfree":
+                self.arrive(op[1])
+
+    def softmax_tile(self, g, j, masked, rescale):
+        """Body of one softmax tile after SFull: returns the waits and checks as a generator."""
+        sb = g & 1
+        assert self.s_buf[sb] == g, f"softmax reads S of tile {g}, buffer holds {self.s_buf[sb]}"
+        self.s_read.add(g)
+        self.arrive(f"SFree{sb}")
+        if j >= 1:
+            yield self.wait("ODone", (g - 1) & 1, g - 1)
+        if masked:
+            n = 2 * g + 1
+            s = n % self.S
+            yield self.wait(f"Full{s}", (n // self.S) & 1, n // self.S)
+            assert self.slot_load[s] == n and self.slot_ready[s] and n not in self.consumed, \
+                f"softmax zeroes V rows of tile {g} in slot {s} holding load {self.slot_load[s]}"
+        assert self.pv_done == g - 1, f"P of tile {g} written while PV of tile {self.pv_done + 1} may read P"
+        self.p_buf = g
+        if j >= 1 and rescale:
+            assert self.pv_done == g - 1, "O rescaled while a PV is in flight"
+        self.arrive("PFull")
+
+
+# -------------------------------------------------- decode_mma_kernel (one item per CTA)
+def run_decode_mma(seed, stages, ntiles, masked, page_ok):
+    sim = Sim(seed, stages)
+    S = stages
+    for s in range(S):
+        sim.bar(f"Full{s}"), sim.bar(f"Empty{s}")
+    for s in range(2):
+        sim.bar(f"SFull{s}"), sim.bar(f"SFree{s}")
+    sim.bar("PFull"), sim.bar("ODone")
+    for g in range(ntiles):
+        sim.tile_item[g] = 0
+    sim.first_tile[0], sim.last_tile[0] = 0, ntiles - 1
+    sim.q_item, sim.q_ready = 0, True  # Q^T is written by the softmax warps before the roles start
+    rng = random.Random(seed + 1)
+    rescale = [rng.random() < 0.3 for _ in range(ntiles)]
+
+    def producer():  # decode_mma.cu, warp 0
+        for n in range(2 * ntiles):
+            slot = n % S
+            if n >= S:
+                yield Sim.wait(f"Empty{slot}", ((n // S) + 1) & 1, n // S - 1)
+            sim.issue_load(n, page_ok[n >> 1])
+            yield ("step",)
+
+    def mma():  # decode_mma.cu, warp 1
+        def issue_pv(t):
+            n, slot = 2 * t + 1, (2 * t + 1) % S
+            yield Sim.wait("PFull", t & 1, t)
+            yield Sim.wait(f"Full{slot}", (n // S) & 1, n // S)
+            sim.tq += [("PV", t), ("commit", f"Empty{slot}"), ("commit", "ODone")]
+
+        for j in range(ntiles):
+            n, slot, sb = 2 * j, (2 * j) % S, j & 1
+            yield Sim.wait(f"Full{slot}", (n // S) & 1, n // S)
+            if j >= 2:
+                yield Sim.wait(f"SFree{sb}", ((j >> 1) + 1) & 1, (j >> 1) - 1)
+            sim.tq += [("S", j, 0), ("commit", f"Empty{slot}"), ("commit", f"SFull{sb}")]
+            if j >= 1:
+                yield from issue_pv(j - 1)
+        yield from issue_pv(ntiles - 1)
+
+    def softmax():  # decode_mma.cu, warps 2..5
+        for j in range(ntiles):
+            yield Sim.wait(f"SFull{j & 1}", (j >> 1) & 1, j >> 1)
+            yield from sim.softmax_tile(j, j, masked[j], rescale[j])
+        yield Sim.wait("ODone", (ntiles - 1) & 1, ntiles - 1)
+        assert sim.pv_done == ntiles - 1
+        sim.epilogue_done.add(0)
+
+    sim.run({"producer": producer(), "mma": mma(), "softmax": softmax(), "tensor": sim.tensor()})
+    assert sim.pv_done == ntiles - 1 and 0 in sim.epilogue_done
+
+
+# ------------------------------------------- decode_persistent_kernel (a stream of items)
+def run_persistent(seed, stages, item_tiles, masked_p):
+    sim = Sim(seed, stages)
+    S = stages
+    for s in range(S):
+        sim.bar(f"Full{s}"), sim.bar(f"Empty{s}")
+    for s in range(2):
+        sim.bar(f"SFull{s}"), sim.bar(f"SFree{s}")
+        sim.bar(f"ItemFull{s}"), sim.bar(f"ItemEmpty{s}", 2)  # MMA thread + softmax (4 warps -> 1 actor)
+        sim.bar(f"QFull{s}")
+    sim.bar("QEmpty"), sim.bar("PFull"), sim.bar("ODone")
+    rng = random.Random(seed + 1)
+    g = 0
+    for i, nt in enumerate(item_tiles):
+        if nt:
+            sim.first_tile[i], sim.last_tile[i] = g, g + nt - 1
+            for _ in range(nt):
+                sim.tile_item[g] = i
+                g += 1
+    total = g
+    masked = [rng.random() < masked_p for _ in range(total)]
+    page_ok = [rng.random() < 0.9 for _ in range(total)]
+    rescale = [rng.random() < 0.3 for _ in range(total)]
+    END = -1
+    items = list(item_tiles) + [END]
+    ring = [None, None]
+
+    def producer():  # decode_persistent.cu, warp 0
+        g = ni = 0
+        for i, nt in enumerate(items):
+            if i >= 2:
+                yield Sim.wait(f"ItemEmpty{i & 1}", ((i >> 1) + 1) & 1, (i >> 1) - 1)
+            ring[i & 1] = (i, nt)
+            sim.arrive(f"ItemFull{i & 1}")
+            if nt == END:
+                break
+            if nt == 0:
+                continue
+            qb = ni & 1
+            if ni >= 1:
+                yield Sim.wait("QEmpty", (ni - 1) & 1, ni - 1)
+            prev = [k for k in sim.last_tile if k < i]
+            if prev:
+                assert sim.last_tile[max(prev)] in sim.s_done_tiles, f"Q of item {i} overwrites Q still read by S"
+            sim.q_item, sim.q_ready = i, False
+
+            def q_land(i=i, qb=qb):
+                assert sim.q_item == i
+                sim.q_ready = True
+                sim.arrive(f"QFull{qb}")
+
+            sim.loads.append(q_land)
+            ni += 1
+            for _j in range(nt):
+                for n in (2 * g, 2 * g + 1):
+                    slot = n % S
+                    if n >= S:
+                        yield Sim.wait(f"Empty{slot}", ((n // S) + 1) & 1, n // S - 1)
+                    sim.issue_load(n, page_ok[g])
+                    yield ("step",)
+                g += 1
+
+    def mma():  # decode_persistent.cu, warp 1
+        g = ni = 0
+
+        def issue_pv(gt):
+            n, slot = 2 * gt + 1, (2 * gt + 1) % S
+            yield Sim.wait("PFull", gt & 1, gt)
+            yield Sim.wait(f"Full{slot}", (n // S) & 1, n // S)
+            sim.tq += [("PV", gt), ("commit", f"Empty{slot}"), ("commit", "ODone")]
+
+        for i in range(len(items)):
+            yield Sim.wait(f"ItemFull{i & 1}", (i >> 1) & 1, i >> 1)
+            idx, nt = ring[i & 1]
+            assert idx == i
+            sim.arrive(f"ItemEmpty{i & 1}")
+            if nt == END:
+                break
+            if nt == 0:
+                continue
+            qb = ni & 1
+            yield Sim.wait(f"QFull{qb}", (ni >> 1) & 1, ni >> 1)
+            ni += 1
+            for j in range(nt):
+                n, slot, sb = 2 * g, (2 * g) % S, g & 1
+                yield Sim.wait(f"Full{slot}", (n // S) & 1, n // S)
+                if g >= 2:
+                    yield Sim.wait(f"SFree{sb}", ((g >> 1) + 1) & 1, (g >> 1) - 1)
+                sim.tq += [("S", g, i), ("commit", f"Empty{slot}"), ("commit", f"SFull{sb}")]
+                if j == nt - 1:
+                    sim.tq.append(("qfree", "QEmpty"))
+                if j >= 1:
+                    yield from issue_pv(g - 1)
+                g += 1
+            yield from issue_pv(g - 1)
+
+    def softmax():  # decode_persistent.cu, warps 2..5
+        g = 0
+        for i in range(len(items)):
+            yield Sim.wait(f"ItemFull{i & 1}", (i >> 1) & 1, i >> 1)
+            idx, nt = ring[i & 1]
+            assert idx == i
+            sim.arrive(f"ItemEmpty{i & 1}")
+            if nt == END:
+                break
+            if nt == 0:
+                continue
+            for j in range(nt):
+                yield Sim.wait(f"SFull{g & 1}", (g >> 1) & 1, g >> 1)
+                yield from sim.softmax_tile(g, j, masked[g], rescale[g])
+                g += 1
+            yield Sim.wait("ODone", (g - 1) & 1, g - 1)
+            assert sim.pv_done == g - 1
+            sim.epilogue_done.add(i)
+
+    sim.run({"producer": producer(), "mma": mma(), "softmax": softmax(), "tensor": sim.tensor()})
+    assert sim.pv_done == total - 1
+    assert sim.epilogue_done == {i for i, nt in enumerate(item_tiles) if nt}
+
+
+# The kernels use 3 slots; 2 and 4 (the old split rings' K/V alternation
+# patterns) and 5 check that the formulas do not depend on the depth.
+@pytest.mark.parametrize("stages", [2, 3, 4, 5])
+def test_decode_mma_ring_protocol(stages):
+    for seed in range(60):
+        rng = random.Random(1000 * stages + seed)
+        ntiles = rng.choice([1, 2, 3, 4, 5, 7, 12])
+        masked = [rng.random() < 0.4 for _ in range(ntiles)]
+        page_ok = [rng.random() < 0.9 for _ in range(ntiles)]
+        run_decode_mma(seed, stages, ntiles, masked, page_ok)
+
+
+@pytest.mark.parametrize("stages", [2, 3, 4, 5])
+def test_persistent_ring_protocol(stages):
+    for seed in range(40):
+        rng = random.Random(2000 * stages + seed)
+        item_tiles = [rng.choice([0, 1, 1, 2, 3, 5]) for _ in range(rng.randint(1, 7))]
+        run_persistent(seed, stages, item_tiles, masked_p=0.4)
+
+
+def test_model_catches_a_wrong_parity():
+    """The model is not vacuous: a producer that waits for the previous
+    load's release instead of the slot's (parity off by one) is caught."""
+
+    def bad(seed):
+        sim = Sim(seed, 3)
+        S = 3
+        for s in range(S):
+            sim.bar(f"Full{s}"), sim.bar(f"Empty{s}")
+
+        def producer():
+            for n in range(8):
+                slot = n % S
+                if n >= S:
+                    yield Sim.wait(f"Empty{slot}", (n // S) & 1, n // S - 1)  # wrong parity
+                sim.issue_load(n, True)
+
+        sim.run({"producer": producer(), "tensor": sim.tensor()})
+
+    with pytest.raises(AssertionError, match="parity formula"):
+        bad(0)
+
+
+def test_model_catches_an_early_reload():
+    """A producer that skips the wait for a slot's release reloads it before
+    the MMA read it, and the model reports the overwrite."""
+    sim = Sim(0, 3)
+    for s in range(3):
+        sim.bar(f"Full{s}"), sim.bar(f"Empty{s}")
+
+    def producer():
+        for n in range(6):
+            sim.issue_load(n, True)
+            yield ("step",)
+
+    with pytest.raises(AssertionError, match="overwrites slot"):
+        sim.run({"producer": producer(), "tensor": sim.tensor()})
