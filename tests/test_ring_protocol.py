@@ -1,4 +1,6 @@
-"""A model check of the decode kernels' mbarrier protocol (CPU only).
+"""A model check of the tensor-core kernels' mbarrier protocols (CPU only):
+the two decode kernels and the one-tile prefill kernel (csrc/prefill_tile.cu,
+modelled further down).
 
 csrc/decode_mma.cu and csrc/decode_persistent.cu stream K and V tiles
 through one ring of kStages shared-memory slots (load n: K of tile n / 2
@@ -45,7 +47,7 @@ class Sim:
         self.bars = {}
         self.waiting = {}  # actor -> (bar, k)
         self.loads = []  # in-flight TMA loads: (callback)
-        self.tq = []  # tensor pipe queue, in issue order
+        self.tqs = {"mma": []}  # tensor-core operations per issuing thread, in issue order
         # data state
         self.slot_load = [None] * stages
         self.slot_ready = [False] * stages
@@ -99,7 +101,7 @@ class Sim:
                 b = self.bars[i[1]]
                 return b.done >= i[2] + 1
             if i[0] == "tensor":
-                return bool(self.tq)
+                return bool(self.tqs[i[1]])
             return True
 
         steps = 0
@@ -115,8 +117,8 @@ class Sim:
                     self.waiting.pop(a, None)
             choices = [("actor", a) for a in instr if ready(a)] + [("load", j) for j in range(len(self.loads))]
             if not choices:
-                unfinished = [a for a, i in instr.items() if i is not None and a != "tensor"]
-                if not unfinished and not self.tq:
+                unfinished = [a for a, i in instr.items() if i is not None and not a.startswith("tensor")]
+                if not unfinished and not any(self.tqs.values()):
                     return
                 raise AssertionError(f"deadlock: {[(a, instr[a]) for a in unfinished]} bars={list(self.bars.values())}")
             kind, x = self.rng.choice(choices)
@@ -124,6 +126,7 @@ class Sim:
                 cb = self.loads.pop(x)
                 cb()
                 continue
+            self.waiting.pop(x, None)  # it has passed its wait before it runs on
             try:
                 instr[x] = next(live[x])
             except StopIteration:
@@ -152,11 +155,15 @@ class Sim:
         assert self.slot_load[s] == n and self.slot_ready[s], f"MMA reads load {n}, slot {s} holds {self.slot_load[s]}"
         self.consumed.add(n)
 
-    def tensor(self):
+    def tensor(self, q="mma"):
+        """One issuing thread's tcgen05 operations: they complete in issue
+        order, and a commit arrives once everything before it completed."""
         while True:
-            yield ("tensor",)
-            op = self.tq.pop(0)
-            if op[0] == "S":
+            yield ("tensor", q)
+            op = self.tqs[q].pop(0)
+            if callable(op):
+                op()
+            elif op[0] == "S":
                 _, g, item = op
                 assert self.q_item == item and self.q_ready, f"S of tile {g} (item {item}) without its Q"
                 self.read_slot(2 * g)
@@ -231,14 +238,14 @@ def run_decode_mma(seed, stages, ntiles, masked, page_ok):
             n, slot = 2 * t + 1, (2 * t + 1) % S
             yield Sim.wait("PFull", t & 1, t)
             yield Sim.wait(f"Full{slot}", (n // S) & 1, n // S)
-            sim.tq += [("PV", t), ("commit", f"Empty{slot}"), ("commit", "ODone")]
+            sim.tqs["mma"] += [("PV", t), ("commit", f"Empty{slot}"), ("commit", "ODone")]
 
         for j in range(ntiles):
             n, slot, sb = 2 * j, (2 * j) % S, j & 1
             yield Sim.wait(f"Full{slot}", (n // S) & 1, n // S)
             if j >= 2:
                 yield Sim.wait(f"SFree{sb}", ((j >> 1) + 1) & 1, (j >> 1) - 1)
-            sim.tq += [("S", j, 0), ("commit", f"Empty{slot}"), ("commit", f"SFull{sb}")]
+            sim.tqs["mma"] += [("S", j, 0), ("commit", f"Empty{slot}"), ("commit", f"SFull{sb}")]
             if j >= 1:
                 yield from issue_pv(j - 1)
         yield from issue_pv(ntiles - 1)
@@ -251,7 +258,7 @@ def run_decode_mma(seed, stages, ntiles, masked, page_ok):
         assert sim.pv_done == ntiles - 1
         sim.epilogue_done.add(0)
 
-    sim.run({"producer": producer(), "mma": mma(), "softmax": softmax(), "tensor": sim.tensor()})
+    sim.run({"producer": producer(), "mma": mma(), "softmax": softmax(), "tensor": sim.tensor("mma")})
     assert sim.pv_done == ntiles - 1 and 0 in sim.epilogue_done
 
 
@@ -324,7 +331,7 @@ def run_persistent(seed, stages, item_tiles, masked_p):
             n, slot = 2 * gt + 1, (2 * gt + 1) % S
             yield Sim.wait("PFull", gt & 1, gt)
             yield Sim.wait(f"Full{slot}", (n // S) & 1, n // S)
-            sim.tq += [("PV", gt), ("commit", f"Empty{slot}"), ("commit", "ODone")]
+            sim.tqs["mma"] += [("PV", gt), ("commit", f"Empty{slot}"), ("commit", "ODone")]
 
         for i in range(len(items)):
             yield Sim.wait(f"ItemFull{i & 1}", (i >> 1) & 1, i >> 1)
@@ -343,9 +350,9 @@ def run_persistent(seed, stages, item_tiles, masked_p):
                 yield Sim.wait(f"Full{slot}", (n // S) & 1, n // S)
                 if g >= 2:
                     yield Sim.wait(f"SFree{sb}", ((g >> 1) + 1) & 1, (g >> 1) - 1)
-                sim.tq += [("S", g, i), ("commit", f"Empty{slot}"), ("commit", f"SFull{sb}")]
+                sim.tqs["mma"] += [("S", g, i), ("commit", f"Empty{slot}"), ("commit", f"SFull{sb}")]
                 if j == nt - 1:
-                    sim.tq.append(("qfree", "QEmpty"))
+                    sim.tqs["mma"].append(("qfree", "QEmpty"))
                 if j >= 1:
                     yield from issue_pv(g - 1)
                 g += 1
@@ -370,7 +377,7 @@ def run_persistent(seed, stages, item_tiles, masked_p):
             assert sim.pv_done == g - 1
             sim.epilogue_done.add(i)
 
-    sim.run({"producer": producer(), "mma": mma(), "softmax": softmax(), "tensor": sim.tensor()})
+    sim.run({"producer": producer(), "mma": mma(), "softmax": softmax(), "tensor": sim.tensor("mma")})
     assert sim.pv_done == total - 1
     assert sim.epilogue_done == {i for i, nt in enumerate(item_tiles) if nt}
 
@@ -412,7 +419,7 @@ def test_model_catches_a_wrong_parity():
                     yield Sim.wait(f"Empty{slot}", (n // S) & 1, n // S - 1)  # wrong parity
                 sim.issue_load(n, True)
 
-        sim.run({"producer": producer(), "tensor": sim.tensor()})
+        sim.run({"producer": producer(), "tensor": sim.tensor("mma")})
 
     with pytest.raises(AssertionError, match="parity formula"):
         bad(0)
@@ -431,4 +438,261 @@ def test_model_catches_an_early_reload():
             yield ("step",)
 
     with pytest.raises(AssertionError, match="overwrites slot"):
-        sim.run({"producer": producer(), "tensor": sim.tensor()})
+        sim.run({"producer": producer(), "tensor": sim.tensor("mma")})
+
+
+# ------------------------------------------------ prefill_tile_kernel (csrc/prefill_tile.cu)
+# Roles: warp 0 publishes items and loads Q (2 stages) and K (2 stages); warp
+# 3 loads V (2 stages); warp 1 issues S = Q K^T into three TMEM S/P buffers;
+# warp 2 fixes V rows past the keys and issues O += P V (a second issuing
+# thread, so S and PV are two independent in-order streams); two softmax
+# warpgroups each take 64 keys of every row and meet at a max exchange per
+# tile (and once more for the row sums); the epilogue warpgroup reads the
+# softmax's row statistics and O. Arrival counts in the model: PFull 8 -> 2
+# (one per half), the exchange 64 -> 2, the item ring's 15 readers -> 6,
+# StatsFull / StatsFree 128 -> 1, OFree 4 -> 1.
+def run_prefill_tile(seed, item_tiles, rescale_p=0.3, page_p=0.9):
+    sim = Sim(seed, 2)
+    sim.tqs = {"s": [], "pv": []}
+    B = sim.bar
+    for s in range(2):
+        for n in ("QFull", "QFree", "KFull", "KEmpty", "VFull", "VEmpty", "ItemFull"):
+            B(f"{n}{s}")
+        B(f"ItemEmpty{s}", 6)
+    for b in range(3):
+        B(f"SFull{b}"), B(f"PVDone{b}"), B(f"PFull{b}", 2)
+    for n in ("ODone", "OFree", "StatsFull", "StatsFree", "Drain", "PVDrain"):
+        B(n)
+    B("Xchg", 2)
+    rng = random.Random(seed + 7)
+    first, g = {}, 0
+    for i, n in enumerate(item_tiles):
+        first[i] = g
+        g += n
+    total = g
+    keyed = [i for i, n in enumerate(item_tiles) if n > 0]
+    item_of = {}
+    for i in keyed:
+        for t in range(first[i], first[i] + item_tiles[i]):
+            item_of[t] = i
+    ok = [rng.random() < page_p for _ in range(total)]
+    rescale = [rng.random() < rescale_p for _ in range(total)]
+    END = -1
+    items = list(item_tiles) + [END]
+    ring = [None, None]
+    st = {
+        "q": [None, None], "q_landed": [False, False], "k": [None, None], "k_landed": [False, False],
+        "v": [None, None], "v_landed": [False, False], "s_done": set(), "pv_done": -1,
+        "buf": [None, None, None], "s_read": {}, "p_written": {}, "o_item": None, "o_read": set(),
+        "stats": None, "stats_read": set(),
+    }
+
+    def load(kind, stage, what, barname, real=True):
+        st[kind][stage], st[kind + "_landed"][stage] = what, False
+
+        def land():
+            assert st[kind][stage] == what
+            st[kind + "_landed"][stage] = True
+            sim.arrive(barname)
+
+        if real:
+            sim.loads.append(land)
+        else:
+            land()
+
+    def take(i):
+        yield Sim.wait(f"ItemFull{i & 1}", (i >> 1) & 1, i >> 1)
+        idx, n = ring[i & 1]
+        assert idx == i
+        sim.arrive(f"ItemEmpty{i & 1}")
+        return n
+
+    def producer():  # warp 0: items, Q and K
+        gt = ix = k_issued = 0
+        for i, n in enumerate(items):
+            if i >= 2:
+                yield Sim.wait(f"ItemEmpty{i & 1}", ((i >> 1) + 1) & 1, (i >> 1) - 1)
+            ring[i & 1] = (i, n)
+            sim.arrive(f"ItemFull{i & 1}")
+            if n == END:
+                break
+            if n == 0:
+                continue
+            qs = ix & 1
+            if ix >= 2:
+                yield Sim.wait(f"QFree{qs}", ((ix >> 1) + 1) & 1, (ix >> 1) - 1)
+                prev = keyed[ix - 2]
+                assert first[prev] + item_tiles[prev] - 1 in st["s_done"], "Q reloaded before its last S"
+            load("q", qs, i, f"QFull{qs}")
+            ix += 1
+            for j in range(n):
+                g, s = gt + j, (gt + j) & 1
+                if g >= 2:
+                    yield Sim.wait(f"KEmpty{s}", ((g >> 1) + 1) & 1, (g >> 1) - 1)
+                    assert g - 2 in st["s_done"], f"K of tile {g} overwrites K of tile {g - 2} before its S"
+                load("k", s, g, f"KFull{s}", ok[g])
+                k_issued = g + 1
+                yield ("step",)
+            gt += n
+        for s in range(2):  # drain
+            if k_issued > s:
+                last = k_issued - 1 - ((k_issued - 1 - s) & 1)
+                yield Sim.wait(f"KFull{s}", ((k_issued - 1 - s) >> 1) & 1, last >> 1)
+            if ix > s:
+                last = ix - 1 - ((ix - 1 - s) & 1)
+                yield Sim.wait(f"QFull{s}", ((ix - 1 - s) >> 1) & 1, last >> 1)
+
+    def v_producer():  # warp 3
+        gt = v_issued = 0
+        for i in range(len(items)):
+            n = yield from take(i)
+            if n == END:
+                break
+            for j in range(n):
+                g, s = gt + j, (gt + j) & 1
+                if g >= 2:
+                    yield Sim.wait(f"VEmpty{s}", ((g >> 1) + 1) & 1, (g >> 1) - 1)
+                    assert st["pv_done"] >= g - 2, f"V of tile {g} overwrites V of tile {g - 2} before its PV"
+                load("v", s, g, f"VFull{s}", ok[g])
+                v_issued = g + 1
+                yield ("step",)
+            gt += n
+        for s in range(2):
+            if v_issued > s:
+                last = v_issued - 1 - ((v_issued - 1 - s) & 1)
+                yield Sim.wait(f"VFull{s}", ((v_issued - 1 - s) >> 1) & 1, last >> 1)
+
+    def s_issuer():  # warp 1
+        gt = ix = 0
+        for i in range(len(items)):
+            n = yield from take(i)
+            if n == END:
+                break
+            if n == 0:
+                continue
+            qs = ix & 1
+            for j in range(n):
+                t, ks, buf = gt + j, (gt + j) & 1, (gt + j) % 3
+                yield Sim.wait(f"KFull{ks}", (t >> 1) & 1, t >> 1)
+                if j == 0:
+                    yield Sim.wait(f"QFull{qs}", (ix >> 1) & 1, ix >> 1)
+                if t >= 3:
+                    yield Sim.wait(f"PVDone{buf}", ((t - 3) // 3) & 1, (t - 3) // 3)
+
+                def exec_s(t=t, ks=ks, buf=buf, qs=qs, i=i):
+                    assert st["q"][qs] == i and st["q_landed"][qs], f"S of tile {t} without item {i}'s Q"
+                    assert st["k"][ks] == t and st["k_landed"][ks], f"S of tile {t} reads K of tile {st['k'][ks]}"
+                    assert t < 3 or st["pv_done"] >= t - 3, f"S of tile {t} overwrites P of tile {t - 3} before its PV"
+                    st["s_done"].add(t)
+                    st["buf"][buf] = t
+                    st["s_read"][t], st["p_written"][t] = set(), set()
+
+                sim.tqs["s"] += [exec_s, lambda b=buf: sim.arrive(f"SFull{b}"), lambda k=ks: sim.arrive(f"KEmpty{k}")]
+                if j == n - 1:
+                    sim.tqs["s"].append(lambda q=qs: sim.arrive(f"QFree{q}"))
+            ix += 1
+            gt += n
+        sim.tqs["s"].append(lambda: sim.arrive("Drain"))
+        yield Sim.wait("Drain", 0, 0)
+
+    def pv_issuer():  # warp 2: V fixer + PV
+        gt = ix = 0
+        for i in range(len(items)):
+            n = yield from take(i)
+            if n == END:
+                break
+            if n == 0:
+                continue
+            for j in range(n):
+                g, s, buf = gt + j, (gt + j) & 1, (gt + j) % 3
+                yield Sim.wait(f"VFull{s}", (g >> 1) & 1, g >> 1)
+                assert st["v"][s] == g and st["v_landed"][s] and st["pv_done"] < g, f"V fixer on tile {g}"
+                if j == 0 and ix > 0:
+                    yield Sim.wait("OFree", (ix - 1) & 1, ix - 1)
+                yield Sim.wait(f"PFull{buf}", (g // 3) & 1, g // 3)
+
+                def exec_pv(g=g, s=s, buf=buf, j=j, i=i):
+                    assert st["v"][s] == g and st["v_landed"][s], f"PV of tile {g} reads V of tile {st['v'][s]}"
+                    assert st["buf"][buf] == g and st["p_written"][g] == {0, 1}, f"PV of tile {g} without its P"
+                    assert st["pv_done"] == g - 1
+                    if j == 0:
+                        prev = [k for k in keyed if k < i]
+                        assert not prev or prev[-1] in st["o_read"], f"item {i}'s first PV before O of {prev[-1]} was read"
+                        st["o_item"] = i
+                    st["pv_done"] = g
+
+                sim.tqs["pv"] += [exec_pv, lambda b=buf: sim.arrive(f"PVDone{b}"), lambda s=s: sim.arrive(f"VEmpty{s}")]
+                if j == n - 1:
+                    sim.tqs["pv"].append(lambda: sim.arrive("ODone"))
+            ix += 1
+            gt += n
+        sim.tqs["pv"].append(lambda: sim.arrive("PVDrain"))
+        yield Sim.wait("PVDrain", 0, 0)
+
+    def softmax(h):  # warps 4..11, half h of every row's keys
+        t = ix = xc = 0
+
+        def exchange():
+            nonlocal xc
+            sim.arrive("Xchg")
+            yield Sim.wait("Xchg", xc & 1, xc)
+            xc += 1
+
+        for i in range(len(items)):
+            n = yield from take(i)
+            if n == END:
+                break
+            if n == 0:
+                continue
+            for j in range(n):
+                buf = t % 3
+                yield Sim.wait(f"SFull{buf}", (t // 3) & 1, t // 3)
+                assert st["buf"][buf] == t and not st["p_written"][t], f"softmax reads S of tile {t}"
+                st["s_read"][t].add(h)
+                yield from exchange()
+                assert st["s_read"][t] == {0, 1}, "P stored over S columns the other half has not read"
+                st["p_written"][t].add(h)
+                if j >= 1 and rescale[t]:
+                    pb = (t - 1) % 3
+                    yield Sim.wait(f"PVDone{pb}", ((t - 1) // 3) & 1, (t - 1) // 3)
+                    assert st["pv_done"] == t - 1, f"O rescaled at tile {t} with PV {st['pv_done']} done"
+                sim.arrive(f"PFull{buf}")
+                t += 1
+            yield from exchange()
+            if h == 0:
+                if ix > 0:
+                    yield Sim.wait("StatsFree", (ix - 1) & 1, ix - 1)
+                    assert keyed[ix - 1] in st["stats_read"], "row statistics overwritten before the epilogue read them"
+                st["stats"] = i
+                sim.arrive("StatsFull")
+            ix += 1
+
+    def epilogue():  # warps 12..15
+        ix = 0
+        for i in range(len(items)):
+            n = yield from take(i)
+            if n == END:
+                break
+            if n == 0:
+                continue
+            yield Sim.wait("StatsFull", ix & 1, ix)
+            assert st["stats"] == i, f"epilogue of item {i} reads statistics of item {st['stats']}"
+            st["stats_read"].add(i)
+            sim.arrive("StatsFree")
+            yield Sim.wait("ODone", ix & 1, ix)
+            assert st["o_item"] == i and st["pv_done"] == first[i] + item_tiles[i] - 1, f"epilogue of item {i}"
+            st["o_read"].add(i)
+            sim.arrive("OFree")
+            ix += 1
+
+    sim.run({"producer": producer(), "v_producer": v_producer(), "s_issuer": s_issuer(), "pv_issuer": pv_issuer(),
+             "softmax0": softmax(0), "softmax1": softmax(1), "epilogue": epilogue(),
+             "tensor_s": sim.tensor("s"), "tensor_pv": sim.tensor("pv")})
+    assert st["pv_done"] == total - 1 and st["o_read"] == set(keyed)
+
+
+def test_prefill_tile_protocol():
+    for seed in range(150):
+        rng = random.Random(3000 + seed)
+        item_tiles = [rng.choice([0, 1, 1, 2, 3, 4, 6]) for _ in range(rng.randint(1, 8))]
+        run_prefill_tile(seed, item_tiles)
