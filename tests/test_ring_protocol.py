@@ -58,7 +58,6 @@ class Sim:
         self.pv_done = -1
         self.q_item = None
         self.q_ready = False
-        self.s_issued_item = {}  # tile -> item
         self.tile_item = {}
         self.first_tile = {}  # item -> first global tile
         self.last_tile = {}
@@ -91,7 +90,6 @@ class Sim:
         instr = {}
         for a, g in live.items():
             instr[a] = next(g, None)
-        done_actors = {a for a, i in instr.items() if i is None}
 
         def ready(a):
             i = instr[a]
