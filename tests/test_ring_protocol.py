@@ -1,6 +1,7 @@
 """A model check of the tensor-core kernels' mbarrier protocols (CPU only):
-the two decode kernels and the one-tile prefill kernel (csrc/prefill_tile.cu,
-modelled further down).
+the two decode kernels, the one-tile prefill kernel (csrc/prefill_tile.cu)
+and the pair prefill kernel (csrc/prefill.cu), the last two modelled further
+down.
 
 csrc/decode_mma.cu and csrc/decode_persistent.cu stream K and V tiles
 through one ring of kStages shared-memory slots (load n: K of tile n / 2
@@ -694,3 +695,286 @@ def test_prefill_tile_protocol():
         rng = random.Random(3000 + seed)
         item_tiles = [rng.choice([0, 1, 1, 2, 3, 4, 6]) for _ in range(rng.randint(1, 8))]
         run_prefill_tile(seed, item_tiles)
+
+
+# ----------------------------------------------------- prefill_kernel (csrc/prefill.cu)
+# Pairs of query tiles A and B (chains x = 0, 1) share every K/V tile of an
+# item. Warp 0 publishes items and loads K (2 stages; an item's first K tile
+# before its Q tiles) and each chain's Q buffer; warp 3 loads V (2 stages)
+# and hands each stage's real-key count to the fixer in shared memory; warp 1
+# issues S_A and S_B per K tile (each S_x single-buffered, so S_x of a tile
+# waits for PV_x of its previous tile); warp 2 zeroes V rows past the keys
+# and issues PV_A and PV_B; one softmax warpgroup per chain; the epilogue
+# reads each chain's statistics and O. Counts in the model: PFull and OFree
+# 4 -> 1, StatsFull / StatsFree 128 -> 1, the item ring's 15 readers -> 6.
+def run_prefill_pair(seed, pairs, rescale_p=0.3, page_p=0.9):
+    sim = Sim(seed, 2)
+    sim.tqs = {"s": [], "pv": []}
+    B = sim.bar
+    for s in range(2):
+        for n in ("QFull", "QFree", "KFull", "KEmpty", "VFull", "VEmpty", "SFull", "PFull", "PVDone", "ODone",
+                  "OFree", "StatsFull", "StatsFree", "ItemFull"):
+            B(f"{n}{s}")
+        B(f"ItemEmpty{s}", 6)
+    B("Drain"), B("PVDrain")
+    rng = random.Random(seed + 11)
+    END = None
+    items = list(pairs) + [END]
+    ring = [None, None]
+    nt_of = [max(a, b) for a, b in pairs]
+    total = sum(nt_of)
+    ok = [rng.random() < page_p for _ in range(total)]
+    # chain tile numbering: (item, j, x) -> t in chain x's order
+    tnum, last_t, first_t, cnt = {}, {}, {}, [0, 0]
+    for i, (na, nb) in enumerate(pairs):
+        for x, n in ((0, na), (1, nb)):
+            for j in range(n):
+                tnum[(i, j, x)] = cnt[x]
+                cnt[x] += 1
+            if n:
+                first_t[(i, x)], last_t[(i, x)] = tnum[(i, 0, x)], tnum[(i, n - 1, x)]
+    rescale = [[rng.random() < rescale_p for _ in range(cnt[x])] for x in range(2)]
+    st = {
+        "q": [None, None], "q_landed": [False, False], "k": [None, None], "k_landed": [False, False],
+        "v": [None, None], "v_landed": [False, False], "v_real": [None, None], "v_real_read": set(),
+        "s_exec": set(), "pv_exec": set(), "sbuf": [None, None], "pv_done": [-1, -1], "o_item": [None, None],
+        "o_read": [set(), set()], "stats": [None, None], "stats_read": [set(), set()],
+    }
+    g_first = []
+    g = 0
+    for i in range(len(pairs)):
+        g_first.append(g)
+        g += nt_of[i]
+
+    def needs(i, j):  # chains that read KV tile j of item i
+        return [x for x in range(2) if j < pairs[i][x]]
+
+    def load(kind, stage, what, barname, real=True):
+        st[kind][stage], st[kind + "_landed"][stage] = what, False
+
+        def land():
+            assert st[kind][stage] == what
+            st[kind + "_landed"][stage] = True
+            sim.arrive(barname)
+
+        if real:
+            sim.loads.append(land)
+        else:
+            land()
+
+    def take(i):
+        yield Sim.wait(f"ItemFull{i & 1}", (i >> 1) & 1, i >> 1)
+        idx, it = ring[i & 1]
+        assert idx == i
+        sim.arrive(f"ItemEmpty{i & 1}")
+        return it
+
+    def producer():  # warp 0
+        gt = k_issued = 0
+        ixq = [0, 0]
+        lastq = [None, None]
+        for i, it in enumerate(items):
+            if i >= 2:
+                yield Sim.wait(f"ItemEmpty{i & 1}", ((i >> 1) + 1) & 1, (i >> 1) - 1)
+            ring[i & 1] = (i, it)
+            sim.arrive(f"ItemFull{i & 1}")
+            if it is END:
+                break
+            nt = nt_of[i]
+            if nt == 0:
+                continue
+
+            def load_k(j, i=i, gt=gt):
+                nonlocal k_issued
+                g, s = gt + j, (gt + j) & 1
+                if g >= 2:
+                    yield Sim.wait(f"KEmpty{s}", ((g >> 1) + 1) & 1, (g >> 1) - 1)
+                    pi, pj = st["k"][s]
+                    assert all((pi, pj, x) in st["s_exec"] for x in needs(pi, pj)), f"K of tile {g} over an unread K"
+                load("k", s, (i, j), f"KFull{s}", ok[g])
+                k_issued = g + 1
+
+            yield from load_k(0)
+            for x in range(2):
+                if pairs[i][x] == 0:
+                    continue
+                if ixq[x] >= 1:
+                    yield Sim.wait(f"QFree{x}", (ixq[x] - 1) & 1, ixq[x] - 1)
+                    pi = lastq[x]
+                    assert (pi, pairs[pi][x] - 1, x) in st["s_exec"], f"Q_{x} reloaded before its last S"
+                load("q", x, i, f"QFull{x}")
+                lastq[x] = i
+                ixq[x] += 1
+            for j in range(1, nt):
+                yield from load_k(j)
+                yield ("step",)
+            gt += nt
+        for s in range(2):
+            if k_issued > s:
+                last = k_issued - 1 - ((k_issued - 1 - s) & 1)
+                yield Sim.wait(f"KFull{s}", ((k_issued - 1 - s) >> 1) & 1, last >> 1)
+            if ixq[s] > 0:
+                yield Sim.wait(f"QFull{s}", (ixq[s] - 1) & 1, ixq[s] - 1)
+
+    def v_producer():  # warp 3
+        gt = v_issued = 0
+        for i in range(len(items)):
+            it = yield from take(i)
+            if it is END:
+                break
+            for j in range(nt_of[i]):
+                g, s = gt + j, (gt + j) & 1
+                if g >= 2:
+                    yield Sim.wait(f"VEmpty{s}", ((g >> 1) + 1) & 1, (g >> 1) - 1)
+                    pi, pj = st["v"][s]
+                    assert all((pi, pj, x) in st["pv_exec"] for x in needs(pi, pj)), f"V of tile {g} over an unread V"
+                    assert (pi, pj) in st["v_real_read"], "real-key count overwritten before the fixer read it"
+                st["v_real"][s] = (i, j)
+                load("v", s, (i, j), f"VFull{s}", ok[g])
+                v_issued = g + 1
+                yield ("step",)
+            gt += nt_of[i]
+        for s in range(2):
+            if v_issued > s:
+                last = v_issued - 1 - ((v_issued - 1 - s) & 1)
+                yield Sim.wait(f"VFull{s}", ((v_issued - 1 - s) >> 1) & 1, last >> 1)
+
+    def s_issuer():  # warp 1
+        gt = 0
+        tx, ixq = [0, 0], [0, 0]
+        for i in range(len(items)):
+            it = yield from take(i)
+            if it is END:
+                break
+            for j in range(nt_of[i]):
+                g, ks = gt + j, (gt + j) & 1
+                yield Sim.wait(f"KFull{ks}", (g >> 1) & 1, g >> 1)
+                for x in range(2):
+                    if j >= pairs[i][x]:
+                        continue
+                    if j == 0:
+                        yield Sim.wait(f"QFull{x}", ixq[x] & 1, ixq[x])
+                    if tx[x] >= 1:
+                        yield Sim.wait(f"PVDone{x}", (tx[x] - 1) & 1, tx[x] - 1)
+
+                    def exec_s(i=i, j=j, x=x, ks=ks, t=tx[x]):
+                        assert st["q"][x] == i and st["q_landed"][x], f"S_{x} of item {i} without its Q"
+                        assert st["k"][ks] == (i, j) and st["k_landed"][ks], f"S_{x} reads K {st['k'][ks]}"
+                        assert st["pv_done"][x] == t - 1, f"S_{x} of tile {t} overwrites P_{x} before its PV"
+                        st["s_exec"].add((i, j, x))
+                        st["sbuf"][x] = ("S", t)
+
+                    sim.tqs["s"] += [exec_s, lambda x=x: sim.arrive(f"SFull{x}")]
+                    if j == pairs[i][x] - 1:
+                        sim.tqs["s"].append(lambda x=x: sim.arrive(f"QFree{x}"))
+                        ixq[x] += 1
+                    tx[x] += 1
+                sim.tqs["s"].append(lambda ks=ks: sim.arrive(f"KEmpty{ks}"))
+            gt += nt_of[i]
+        sim.tqs["s"].append(lambda: sim.arrive("Drain"))
+        yield Sim.wait("Drain", 0, 0)
+
+    def pv_issuer():  # warp 2: V fixer + PV
+        gt = 0
+        tx, ixo = [0, 0], [0, 0]
+        prev_item = [None, None]
+        for i in range(len(items)):
+            it = yield from take(i)
+            if it is END:
+                break
+            for j in range(nt_of[i]):
+                g, s = gt + j, (gt + j) & 1
+                yield Sim.wait(f"VFull{s}", (g >> 1) & 1, g >> 1)
+                assert st["v_real"][s] == (i, j), "fixer reads another tile's real-key count"
+                st["v_real_read"].add((i, j))
+                assert st["v"][s] == (i, j) and st["v_landed"][s], f"fixer zeroes V {st['v'][s]}"
+                assert not any((i, j, x) in st["pv_exec"] for x in range(2)), "V rows zeroed after a PV read them"
+                for x in range(2):
+                    if j >= pairs[i][x]:
+                        continue
+                    if j == 0 and ixo[x] > 0:
+                        yield Sim.wait(f"OFree{x}", (ixo[x] - 1) & 1, ixo[x] - 1)
+                    yield Sim.wait(f"PFull{x}", tx[x] & 1, tx[x])
+
+                    def exec_pv(i=i, j=j, x=x, s=s, t=tx[x], prev=prev_item[x]):
+                        assert st["sbuf"][x] == ("P", t), f"PV_{x} of tile {t} reads {st['sbuf'][x]}"
+                        assert st["v"][s] == (i, j) and st["v_landed"][s], f"PV_{x} reads V {st['v'][s]}"
+                        assert st["pv_done"][x] == t - 1
+                        if j == 0:
+                            assert prev is None or prev in st["o_read"][x], f"O_{x} restarted before item {prev} was read"
+                            st["o_item"][x] = i
+                        st["pv_exec"].add((i, j, x))
+                        st["pv_done"][x] = t
+
+                    sim.tqs["pv"] += [exec_pv, lambda x=x: sim.arrive(f"PVDone{x}")]
+                    if j == pairs[i][x] - 1:
+                        sim.tqs["pv"].append(lambda x=x: sim.arrive(f"ODone{x}"))
+                        ixo[x] += 1
+                        prev_item[x] = i
+                    tx[x] += 1
+                sim.tqs["pv"].append(lambda s=s: sim.arrive(f"VEmpty{s}"))
+            gt += nt_of[i]
+        sim.tqs["pv"].append(lambda: sim.arrive("PVDrain"))
+        yield Sim.wait("PVDrain", 0, 0)
+
+    def softmax(x):  # warps 4..7 (A) or 8..11 (B)
+        t = ix = 0
+        for i in range(len(items)):
+            it = yield from take(i)
+            if it is END:
+                break
+            n = pairs[i][x]
+            if n == 0:
+                continue
+            for j in range(n):
+                yield Sim.wait(f"SFull{x}", t & 1, t)
+                assert st["sbuf"][x] == ("S", t), f"softmax {x} reads {st['sbuf'][x]} for tile {t}"
+                if j >= 1 and rescale[x][t]:
+                    yield Sim.wait(f"PVDone{x}", (t - 1) & 1, t - 1)
+                    assert st["pv_done"][x] == t - 1, f"O_{x} rescaled at tile {t} with PV {st['pv_done'][x]}"
+                st["sbuf"][x] = ("P", t)
+                sim.arrive(f"PFull{x}")
+                t += 1
+            if ix > 0:
+                yield Sim.wait(f"StatsFree{x}", (ix - 1) & 1, ix - 1)
+                assert st["stats"][x] in st["stats_read"][x], f"statistics {x} overwritten before they were read"
+            st["stats"][x] = i
+            sim.arrive(f"StatsFull{x}")
+            ix += 1
+
+    def epilogue():  # warps 12..15
+        ixo = [0, 0]
+        for i in range(len(items)):
+            it = yield from take(i)
+            if it is END:
+                break
+            for x in range(2):
+                if pairs[i][x] == 0:
+                    continue
+                yield Sim.wait(f"StatsFull{x}", ixo[x] & 1, ixo[x])
+                assert st["stats"][x] == i
+                st["stats_read"][x].add(i)
+                sim.arrive(f"StatsFree{x}")
+                yield Sim.wait(f"ODone{x}", ixo[x] & 1, ixo[x])
+                assert st["o_item"][x] == i and st["pv_done"][x] == last_t[(i, x)], f"epilogue {x} of item {i}"
+                st["o_read"][x].add(i)
+                sim.arrive(f"OFree{x}")
+                ixo[x] += 1
+
+    sim.run({"producer": producer(), "v_producer": v_producer(), "s_issuer": s_issuer(), "pv_issuer": pv_issuer(),
+             "softmax0": softmax(0), "softmax1": softmax(1), "epilogue": epilogue(),
+             "tensor_s": sim.tensor("s"), "tensor_pv": sim.tensor("pv")})
+    for x in range(2):
+        assert st["pv_done"][x] == cnt[x] - 1
+        assert st["o_read"][x] == {i for i, p in enumerate(pairs) if p[x]}
+
+
+def test_prefill_pair_protocol():
+    for seed in range(150):
+        rng = random.Random(4000 + seed)
+        pairs = []
+        for _ in range(rng.randint(1, 7)):
+            a = rng.choice([0, 1, 2, 3, 5])
+            b = rng.choice([0, a, a, a + 1, max(0, a - 1)])
+            pairs.append((a, b))
+        run_prefill_pair(seed, pairs)
