@@ -121,8 +121,12 @@ int nvb_num_splits(int batch, int q_heads, int kv_heads, int max_k, int num_sms)
  * Every rank must make the call with the same epoch; a rank that does not
  * leaves the others' barrier to give up after about two seconds, recording
  * device error 7 (nvb_device_error). Output buffers are written by all
- * ranks: alternate two of them between steps, so that no rank writes a
- * buffer another rank may still be reading. */
+ * ranks: alternate two of them between steps, and read step n's output (or
+ * enqueue its readers on `stream`) before this rank's next call. A peer one
+ * step ahead stores step n + 2 into the same buffer as soon as this rank's
+ * step n + 1 has exchanged its epoch, which is before work enqueued after
+ * that call runs. The same holds for the two output sets of the capturable
+ * form below. */
 int nvb_paged_decode_gather(void* stream, const void* q, const void* k, const void* v, void* out_local,
                             const int* cu_q, const int* kv_lens, const int* block_table, int batch, int max_k,
                             int q_heads, int kv_heads, int block_size, int table_stride, int num_blocks,

@@ -101,8 +101,10 @@ class KvHeadShardedDecode:
     [num_blocks, block_size, kv_local, 128]; `q_local` is
     [batch, q_local, 128] (the query heads of this rank's kv heads).
     fused=True (default): combine and all-gather in one kernel through peer
-    memory; the returned tensor is one of two output buffers used in turn
-    and stays valid until the call after next. `capture` records one such
+    memory; the returned tensor is one of two output buffers used in turn.
+    Read it (or enqueue its readers on the current stream) before this
+    rank's next call: a peer stores the step after that into the same
+    buffer as soon as this rank's next step has signalled. `capture` records one such
     step in a CUDA graph and `replay` runs it (every rank must call and
     replay in the same order). fused=False: NCCL all-gather.
     Call close() before destroying the process group."""
