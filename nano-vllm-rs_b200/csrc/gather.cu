@@ -7,9 +7,11 @@
 // the KV cache. Every rank then needs the whole [batch, q_heads, 128] output.
 // Instead of a separate collective after the decode, the combine kernel below
 // stores each (sequence, head) result straight into every rank's output
-// buffer (peer stores over NVLink through CUDA IPC mappings), and a one-warp
-// barrier kernel exchanges a per-step epoch flag with every peer, so that when
-// a rank's stream moves on, all peers' stores into its buffer have landed.
+// buffer (peer stores over NVLink through CUDA IPC mappings), and a per-step
+// epoch flag is exchanged with every peer (by a one-warp barrier kernel in
+// the host-epoch form, by the combine's last CTA in the capturable form), so
+// that when a rank's stream moves on, all peers' stores into its buffer have
+// landed.
 //
 // The reference is single-GPU (its README: no NCCL, MPI or tensor
 // parallelism); this path has no counterpart there. No TMA, no multicast and
