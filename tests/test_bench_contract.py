@@ -38,3 +38,18 @@ def test_reference_arm_other_ranks_exit_quietly():
                           "2", "--warmup", "1"], cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
     assert run.returncode == 0, run.stderr[-2000:]
     assert not [ln for ln in run.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_roofline_traffic_comes_from_the_committed_profile():
+    # roofline.traffic is read from profiles/decode_config3_ncu.md (an ncu
+    # capture scaled to a full config-3 launch): it must parse, and DRAM bytes
+    # may exceed the algorithmic bytes of one launch only by a few per cent
+    # (the kernel reads every K/V byte once).
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_for_test", ROOT / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    traffic = bench.profile_traffic()
+    algorithmic = bench.BATCH * bench.bytes_per_seq()
+    assert traffic is not None and 1.0 <= traffic / algorithmic <= 1.02, (traffic, algorithmic)
