@@ -76,3 +76,18 @@ def test_native_entry_rejects_unsupported_shapes_on_host(nvb):
     assert b"multiple of 32" in lib.nvb_last_error()
     assert lib.nvb_qkv_rope_cached(P(0), nz, nz, nz, nz, nz, nz, nz, nz, 1, 4, 2, 128, 256, 1, ctypes.c_float(0.0),
                                    nz, 16) == -1
+
+
+def test_integration_notes_name_only_declared_entry_points():
+    # Every C entry point that INTEGRATION.md tells a maintainer to bind (the
+    # Rust extern block and the functions named in the text) is declared in
+    # a header under include/.
+    text = (ROOT / "INTEGRATION.md").read_text()
+    named = set(re.findall(r"\bfn (nvb[a-z0-9_]*)\s*\(", text)) | set(re.findall(r"`(nvbe?h?_[a-z0-9_]+)`", text))
+    declared_all = set()
+    for h in (ROOT / "include").glob("*.h"):
+        src = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        declared_all |= set(re.findall(r"\b(nvb[a-z]?_[a-z0-9_]+)\s*\(", src))
+    assert named, "no entry points found in INTEGRATION.md"
+    missing = sorted(n for n in named if n not in declared_all)
+    assert not missing, missing
